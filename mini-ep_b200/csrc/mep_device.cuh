@@ -1,0 +1,70 @@
+// Device helpers: element conversions that mirror torch's CPU rounding,
+// system-scope flag signalling with bounded waits.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include "mep_internal.h"
+
+namespace mep {
+
+template <typename T> struct Elt;
+template <> struct Elt<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+  // value as the model dtype would hold it (identity for fp32)
+  static __device__ __forceinline__ float round(float v) { return v; }
+};
+template <> struct Elt<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ float round(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+  }
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void set_err(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// Spin until *flag has reached `target` (wrap-safe compare), for at most
+// wc.timeout_ns. Gives up early when another wait already failed, so one
+// missing peer costs one timeout rather than one per kernel. Returns true
+// when the flag arrived.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t target, int errcode,
+                                          const WaitCfg& wc) {
+  if ((int32_t)(ld_acquire_sys(flag) - target) >= 0) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if ((int32_t)(ld_acquire_sys(flag) - target) >= 0) return true;
+    __nanosleep(64);
+    if ((it & 255u) == 255u) {
+      if (wc.err && *(volatile int*)wc.err != 0) return false;
+      if (globaltimer_ns() - t0 > wc.timeout_ns) {
+        set_err(wc.err, errcode);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+}  // namespace mep

@@ -1,0 +1,122 @@
+// Internal declarations shared by the CUDA translation units of libminiep_b200.
+// Nothing here is part of the C ABI (include/miniep_b200.h is).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+namespace mep {
+
+constexpr int kMaxWorld = 8;      // ranks of one NVLink/NVSwitch box
+constexpr int kMaxExperts = 128;  // experts per layer
+constexpr int kMaxTopk = 16;
+constexpr int kRowAlign = 128;    // expert segments in the receive buffer start on 128-row boundaries
+constexpr int kRouteChunkTokens = 256;  // tokens per CTA in the routing scan
+
+enum DType : int { kF32 = 0, kBF16 = 1 };
+
+// Device-side error word values (written to host-mapped memory).
+enum DevErr : int {
+  kErrNone = 0,
+  kErrWaitCounts = 1,     // timed out waiting for a peer's routing counts
+  kErrWaitData = 2,       // timed out waiting for a peer's dispatched rows
+  kErrWaitDone = 3,       // timed out waiting for a peer's expert outputs
+  kErrExpertId = 4,       // routing index outside [0, E)
+  kErrCapacity = 5,       // a receive buffer would overflow
+  kErrNotResident = 6,    // entry routed to a rank that does not hold the expert
+  kErrWaitDebug = 7,      // the debug wait entry point timed out
+  kErrPipeline = 8,       // a tensor-core pipeline barrier timed out
+};
+
+// Receive-side layout and send offsets for one layer step, computed on the
+// device after the routing counts of every rank are known.
+struct Layout {
+  int n_local;                       // experts resident on this rank
+  int total_rows;                    // padded rows of the receive buffer in use
+  int total_mtiles;                  // 128-row tiles over all local segments
+  int recv_rows;                     // real (unpadded) rows received
+  int seg_base[kMaxExperts];         // first padded row of local expert j
+  int seg_rows[kMaxExperts];         // rows of local expert j
+  int tile_prefix[kMaxExperts + 1];  // first 128-row tile of local expert j
+  int local_expert[kMaxExperts];     // global id of local expert j
+  int dst_off[kMaxWorld * kMaxExperts];  // [d][e]: first row this rank writes at rank d for expert e
+};
+
+// Pointers every rank can reach (own and peers' symmetric buffers).
+struct PeerPtrs {
+  void* recv_x[kMaxWorld];
+  int32_t* recv_meta[kMaxWorld];
+  void* yk[kMaxWorld];
+  int32_t* cnt_in[kMaxWorld];
+  uint32_t* flags[kMaxWorld];  // [0,W) counts, [W,2W) data, [2W,3W) done
+};
+
+struct WaitCfg {
+  int* err;                 // host-mapped error word
+  unsigned long long timeout_ns;
+};
+
+// ---------------------------------------------------------------- router
+void launch_router(int dtype, const void* x, const void* router_w, const float* bias,
+                   int64_t n, int hidden, int experts, int topk, int64_t* idx_out,
+                   void* gate_out, float* logits_out, cudaStream_t st);
+
+// ---------------------------------------------------------------- routing
+void launch_route(int64_t n, int topk, int experts, int world, int rank,
+                  const int64_t* topk_idx, const uint8_t* valid,
+                  const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,
+                  int64_t* route_counts_l, int32_t* chunk_hist, int32_t* ent_dest,
+                  int32_t* ent_grp, int32_t* my_counts, const PeerPtrs& peers,
+                  uint32_t seq, WaitCfg wc, cudaStream_t st);
+
+void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids,
+                      const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,
+                      int32_t* chunk_hist, int32_t* ent_dest, int32_t* ent_grp,
+                      int32_t* my_counts, int64_t* dest_out, WaitCfg wc, cudaStream_t st);
+
+void launch_layout(int world, int rank, int experts, const int32_t* owners_l,
+                   const int32_t* nrep_l, const int32_t* cnt_in_local,
+                   const uint32_t* flags_local, int64_t* recv_per_layer_l, int64_t cap_rows,
+                   Layout* layout, uint32_t seq, WaitCfg wc, cudaStream_t st);
+
+// ---------------------------------------------------------------- movement
+void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int rank,
+                     const void* x, const int64_t* topk_idx, const int32_t* ent_dest,
+                     const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
+                     unsigned int* done_ctr, uint32_t seq, int num_sms, cudaStream_t st);
+
+void launch_wait_flags(const uint32_t* flags_local, int first, int world, uint32_t seq,
+                       int errcode, WaitCfg wc, cudaStream_t st);
+
+void launch_combine(int dtype, int64_t n, int topk, int hidden, int world,
+                    const void* yk_local, const void* topk_gate, const uint8_t* valid,
+                    const void* h, float residual_multiplier, void* out, void* h_out,
+                    const uint32_t* flags_local, uint32_t seq, WaitCfg wc, int num_sms,
+                    cudaStream_t st);
+
+// ---------------------------------------------------------------- expert FFN
+struct FfnArgs {
+  int dtype;
+  int hidden, inter, world, rank;
+  int64_t cap_rows;
+  const void* recv_x;       // (cap_rows, H)  local receive buffer
+  const int32_t* recv_meta; // (cap_rows,)    (src << 24) | entry
+  void* act;                // (cap_rows, I)  SwiGLU activations
+  const void* w_in;         // (E_l, 2I, H)
+  const void* w_out;        // (E_l, H, I)
+  const Layout* layout;
+  PeerPtrs peers;
+  unsigned int* done_ctr;
+  uint32_t seq;
+  int num_sms;
+  int force_simt;           // 1: run the CUDA-core kernels even for bf16
+  int n_local_weights;      // leading extent of w_in / w_out
+  int* err;                 // host-mapped device error word
+};
+// Returns 0 on success, else a cudaError_t value or a negative code.
+int launch_ffn(const FfnArgs& a, cudaStream_t st);
+bool tc_shape_ok(int hidden, int inter);
+int tc_init();  // resolves cuTensorMapEncodeTiled; 0 ok
+
+}  // namespace mep

@@ -1,0 +1,204 @@
+// Dispatch and combine.
+//
+// Dispatch (ep.py:223-226): every kept entry's hidden row is stored straight
+// into the destination rank's receive buffer at its final, expert-grouped
+// position (peer stores over NVLink for remote ranks, local stores for this
+// rank), together with a 4-byte tag (source rank, flat entry index) that
+// tells the destination where the expert output must go back to. There is no
+// send-side staging buffer and no separate permute pass.
+//
+// Combine (ep.py:234-242, scatter_combine modeling.py:120-128, residual
+// modeling.py:197): the expert outputs arrive in this rank's (token, slot)
+// landing buffer; each token sums gate * y over its slots in slot order
+// 0..k-1 in fp32 (each product rounded to the model dtype first, as the
+// reference multiplies in the model dtype), rounds once, and optionally adds
+// the scaled residual. No atomics, so the result does not depend on the
+// placement or on the number of ranks.
+#include <cstdint>
+#include "mep_device.cuh"
+
+namespace mep {
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+// Signal "this kernel's stores are done" to every rank: flag slot
+// [flag_base + rank] on each peer is raised to `seq` by the last CTA to finish.
+__device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const PeerPtrs& peers,
+                                                 int world, int rank, int flag_base, uint32_t seq) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(done_ctr, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int d = 0; d < world; ++d) st_release_sys(peers.flags[d] + flag_base + rank, seq);
+      *done_ctr = 0u;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) k_dispatch(int64_t n, int topk, int row_bytes, int world,
+                                                  int rank, const uint8_t* __restrict__ x,
+                                                  const int64_t* __restrict__ topk_idx,
+                                                  const int32_t* __restrict__ ent_dest,
+                                                  const int32_t* __restrict__ ent_grp,
+                                                  const Layout* __restrict__ lay, PeerPtrs peers,
+                                                  unsigned int* done_ctr, uint32_t seq) {
+  const int lane = lane_id();
+  const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t m = n * topk;
+  const int vec = row_bytes >> 4;
+  for (int64_t f = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); f < m; f += warps_total) {
+    const int d = ent_dest[f];
+    if (d < 0) continue;
+    const int e = (int)topk_idx[f];
+    const int off = lay->dst_off[d * kMaxExperts + e];
+    if (off < 0) continue;  // destination would overflow: error already raised
+    const int64_t pos = (int64_t)off + ent_grp[f];
+    const uint4* src = reinterpret_cast<const uint4*>(x + (f / topk) * (int64_t)row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peers.recv_x[d]) + pos * row_bytes);
+    for (int i = lane; i < vec; i += 32) dst[i] = __ldg(src + i);
+    if (lane == 0) peers.recv_meta[d][pos] = (rank << 24) | (int32_t)f;
+  }
+  grid_done_signal(done_ctr, peers, world, rank, world, seq);
+}
+
+__global__ void k_wait_flags(const uint32_t* flags, int first, int world, uint32_t seq, int code,
+                             WaitCfg wc) {
+  if (threadIdx.x < world) wait_flag(flags + first + threadIdx.x, seq, code, wc);
+}
+
+template <typename T>
+struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& v, float (&o)[Vec16<T>::N]);
+template <>
+__device__ __forceinline__ void unpack16<float>(const uint4& v, float (&o)[4]) {
+  o[0] = __uint_as_float(v.x);
+  o[1] = __uint_as_float(v.y);
+  o[2] = __uint_as_float(v.z);
+  o[3] = __uint_as_float(v.w);
+}
+template <>
+__device__ __forceinline__ void unpack16<bf16>(const uint4& v, float (&o)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    o[2 * i] = __uint_as_float(w[i] << 16);
+    o[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const float (&o)[Vec16<T>::N]);
+template <>
+__device__ __forceinline__ uint4 pack16<float>(const float (&o)[4]) {
+  return make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]),
+                    __float_as_uint(o[3]));
+}
+template <>
+__device__ __forceinline__ uint4 pack16<bf16>(const float (&o)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&p);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int world,
+                                                 const T* __restrict__ yk,
+                                                 const T* __restrict__ gate,
+                                                 const uint8_t* __restrict__ valid,
+                                                 const T* __restrict__ h, float rm,
+                                                 T* __restrict__ out, T* __restrict__ h_out,
+                                                 const uint32_t* flags, uint32_t seq, WaitCfg wc) {
+  constexpr int V = Vec16<T>::N;
+  if (threadIdx.x < world) wait_flag(flags + 2 * world + threadIdx.x, seq, kErrWaitDone, wc);
+  __syncthreads();
+  const int lane = lane_id();
+  const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int nvec = H / V;
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); t < n; t += warps_total) {
+    const bool keep = valid == nullptr || valid[t] != 0;
+    float g[kMaxTopk];
+    if (keep)
+      for (int s = 0; s < topk; ++s) g[s] = Elt<T>::to_f(gate[t * topk + s]);
+    for (int c = lane; c < nvec; c += 32) {
+      float acc[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) acc[i] = 0.f;
+      if (keep) {
+        for (int s = 0; s < topk; ++s) {
+          const uint4 raw = reinterpret_cast<const uint4*>(yk + (t * topk + s) * (int64_t)H)[c];
+          float y[V];
+          unpack16<T>(raw, y);
+#pragma unroll
+          for (int i = 0; i < V; ++i) acc[i] += Elt<T>::round(y[i] * g[s]);
+        }
+      }
+      float o[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) o[i] = Elt<T>::round(acc[i]);
+      if (out) reinterpret_cast<uint4*>(out + t * (int64_t)H)[c] = pack16<T>(o);
+      if (h_out) {
+        const uint4 hr = reinterpret_cast<const uint4*>(h + t * (int64_t)H)[c];
+        float hv[V];
+        unpack16<T>(hr, hv);
+        float r[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) r[i] = hv[i] + Elt<T>::round(o[i] * rm);
+        reinterpret_cast<uint4*>(h_out + t * (int64_t)H)[c] = pack16<T>(r);
+      }
+    }
+  }
+}
+
+}  // namespace
+
+void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int rank,
+                     const void* x, const int64_t* topk_idx, const int32_t* ent_dest,
+                     const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
+                     unsigned int* done_ctr, uint32_t seq, int num_sms, cudaStream_t st) {
+  const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
+  const int64_t m = n * topk;
+  int64_t blocks = (m + 7) / 8;
+  if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
+  if (blocks < 1) blocks = 1;
+  k_dispatch<<<(unsigned)blocks, 256, 0, st>>>(n, topk, row_bytes, world, rank,
+                                               static_cast<const uint8_t*>(x), topk_idx, ent_dest,
+                                               ent_grp, layout, peers, done_ctr, seq);
+}
+
+void launch_wait_flags(const uint32_t* flags_local, int first, int world, uint32_t seq,
+                       int errcode, WaitCfg wc, cudaStream_t st) {
+  k_wait_flags<<<1, 32, 0, st>>>(flags_local, first, world, seq, errcode, wc);
+}
+
+void launch_combine(int dtype, int64_t n, int topk, int hidden, int world, const void* yk_local,
+                    const void* topk_gate, const uint8_t* valid, const void* h,
+                    float residual_multiplier, void* out, void* h_out, const uint32_t* flags_local,
+                    uint32_t seq, WaitCfg wc, int num_sms, cudaStream_t st) {
+  int64_t blocks = (n + 7) / 8;
+  if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
+  if (blocks < 1) blocks = 1;
+  if (dtype == kBF16)
+    k_combine<bf16><<<(unsigned)blocks, 256, 0, st>>>(
+        n, topk, hidden, world, static_cast<const bf16*>(yk_local),
+        static_cast<const bf16*>(topk_gate), valid, static_cast<const bf16*>(h),
+        residual_multiplier, static_cast<bf16*>(out), static_cast<bf16*>(h_out), flags_local, seq,
+        wc);
+  else
+    k_combine<float><<<(unsigned)blocks, 256, 0, st>>>(
+        n, topk, hidden, world, static_cast<const float*>(yk_local),
+        static_cast<const float*>(topk_gate), valid, static_cast<const float*>(h),
+        residual_multiplier, static_cast<float*>(out), static_cast<float*>(h_out), flags_local,
+        seq, wc);
+}
+
+}  // namespace mep

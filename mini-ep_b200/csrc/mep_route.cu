@@ -1,0 +1,284 @@
+// Routing of entries to ranks, without a host round trip:
+//   * per-expert histogram of the kept entries            (ep.py:216-217, route_counts)
+//   * stable occurrence index of every entry within its expert, in flat
+//     (token-major, slot-minor) order over kept entries   (ep.py:86-93)
+//   * destination rank by replica round-robin,
+//     replica = (rr[e] + occurrence) % n_rep[e], then rr[e] += count[e]   (ep.py:76-96)
+//   * per-(destination, expert) counts published to every rank, which is the
+//     counts exchange of the reference (ep.py:120-124) done as peer stores
+//   * the receive layout (expert segments in sorted local-expert order, each
+//     source's rows in rank order inside a segment) computed identically on
+//     every rank from the exchanged counts.
+// flatten_topk's masking (modeling.py:107-117) is folded in: entries of
+// invalid tokens are not counted, not routed, not sent.
+//
+// Index within a (destination, expert) group: the entries of expert e with
+// occurrence w go to replica slot (rr0 + w) % n; the earlier entries with the
+// same slot are w - n, w - 2n, ... >= 0, so the group index is w / n.
+#include <cstdint>
+#include "mep_device.cuh"
+
+namespace mep {
+namespace {
+
+constexpr int kRouteThreads = kRouteChunkTokens;  // one token per thread in the histogram pass
+constexpr int kRouteWarps = kRouteThreads / 32;
+
+__device__ __forceinline__ int entry_expert(const int64_t* idx, const uint8_t* valid, int64_t f,
+                                            int k, int64_t n, int E, int* err) {
+  const int64_t t = f / k;
+  if (t >= n) return -1;
+  if (valid && !valid[t]) return -1;
+  const int64_t e = idx[f];
+  if (e < 0 || e >= E) {
+    set_err(err, kErrExpertId);
+    return -1;
+  }
+  return (int)e;
+}
+
+__global__ void __launch_bounds__(kRouteThreads) k_route_hist(int64_t n, int k, int E,
+                                                              const int64_t* __restrict__ idx,
+                                                              const uint8_t* __restrict__ valid,
+                                                              int32_t* __restrict__ chunk_hist,
+                                                              int* err) {
+  __shared__ int h[kMaxExperts];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
+  __syncthreads();
+  const int64_t t = (int64_t)blockIdx.x * kRouteChunkTokens + threadIdx.x;
+  if (t < n) {
+    for (int s = 0; s < k; ++s) {
+      const int e = entry_expert(idx, valid, t * k + s, k, n, E, err);
+      if (e >= 0) atomicAdd(&h[e], 1);
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_hist[(int64_t)blockIdx.x * E + e] = h[e];
+}
+
+// Occurrence index (stable, flat order) -> destination rank and index within
+// the (destination, expert) group. Entries of one chunk are walked by warps in
+// rounds of 32 consecutive flat entries; lanes holding the same expert are
+// ranked with __match_any_sync.
+__global__ void __launch_bounds__(kRouteThreads) k_route_rank(
+    int64_t n, int k, int E, const int64_t* __restrict__ idx, const uint8_t* __restrict__ valid,
+    const int32_t* __restrict__ owners, const int32_t* __restrict__ nrep,
+    const int64_t* __restrict__ rr, const int32_t* __restrict__ chunk_hist,
+    int32_t* __restrict__ ent_dest, int32_t* __restrict__ ent_grp) {
+  __shared__ int base[kMaxExperts];
+  __shared__ int wcnt[kRouteWarps][kMaxExperts];
+  __shared__ int wbase[kRouteWarps][kMaxExperts];
+  __shared__ int rr_mod[kMaxExperts];
+  const int wp = warp_id(), lane = lane_id();
+  const int chunk = blockIdx.x;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int b = 0;
+    for (int c = 0; c < chunk; ++c) b += chunk_hist[(int64_t)c * E + e];
+    base[e] = b;
+    rr_mod[e] = (int)(rr[e] % nrep[e]);
+    for (int w = 0; w < kRouteWarps; ++w) wcnt[w][e] = 0;
+  }
+  __syncthreads();
+  // this warp's entries: tokens [t0, t0+32) -> flat entries [t0*k, (t0+32)*k)
+  const int64_t t0 = (int64_t)chunk * kRouteChunkTokens + wp * 32;
+  const int64_t f0 = t0 * k;
+  for (int r = 0; r < k; ++r) {
+    const int e = entry_expert(idx, valid, f0 + r * 32 + lane, k, n, E, nullptr);
+    if (e >= 0) atomicAdd(&wcnt[wp][e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kRouteWarps; ++w) {
+      wbase[w][e] = run;
+      run += wcnt[w][e];
+      wcnt[w][e] = 0;  // reused as the running count of pass 2
+    }
+  }
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int r = 0; r < k; ++r) {
+    const int64_t f = f0 + r * 32 + lane;
+    const int e = entry_expert(idx, valid, f, k, n, E, nullptr);
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank_in_round = __popc(peers & lt_mask);
+    int dest = -1, grp = 0;
+    if (e >= 0) {
+      const int within = base[e] + wbase[wp][e] + wcnt[wp][e] + rank_in_round;
+      const int nr = nrep[e];
+      const int slot = (rr_mod[e] + within) % nr;
+      dest = owners[e * kMaxWorld + slot];
+      grp = within / nr;
+    }
+    __syncwarp();
+    if (e >= 0 && rank_in_round == 0) wcnt[wp][e] += __popc(peers);
+    __syncwarp();
+    if (f < n * k) {
+      ent_dest[f] = dest;
+      ent_grp[f] = grp;
+    }
+  }
+}
+
+// Totals, round-robin state, stats, per-(destination, expert) counts; when
+// `publish`, the counts are stored into every rank's exchange slot for this
+// source and the rank's counts flag is raised. The round-robin state of a
+// layer without any replicated expert is left alone, like the reference's
+// fast path (ep.py:84-85); it cannot affect any destination there.
+__global__ void __launch_bounds__(256) k_route_finalize(
+    int nchunks, int E, int world, int rank, const int32_t* __restrict__ owners,
+    const int32_t* __restrict__ nrep, int64_t* __restrict__ rr, int64_t* __restrict__ route_counts,
+    const int32_t* __restrict__ chunk_hist, int32_t* __restrict__ my_counts, PeerPtrs peers,
+    uint32_t seq, int publish) {
+  __shared__ int cnt[kMaxWorld * kMaxExperts];
+  __shared__ int any_rep;
+  if (threadIdx.x == 0) any_rep = 0;
+  for (int i = threadIdx.x; i < world * E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    if (nrep[e] > 1) any_rep = 1;
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int c = 0;
+    for (int ch = 0; ch < nchunks; ++ch) c += chunk_hist[(int64_t)ch * E + e];
+    const int nr = nrep[e];
+    const int rr0 = (int)(rr[e] % nr);
+    for (int j = 0; j < nr; ++j) {
+      const int d = owners[e * kMaxWorld + j];
+      const int w0 = ((j - rr0) % nr + nr) % nr;
+      cnt[d * E + e] = c > w0 ? (c - w0 - 1) / nr + 1 : 0;
+    }
+    if (any_rep) rr[e] += c;
+    if (route_counts) route_counts[e] += c;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < world * E; i += blockDim.x) my_counts[i] = cnt[i];
+  if (!publish) return;
+  for (int d = 0; d < world; ++d) {
+    int32_t* dst = peers.cnt_in[d] + (int64_t)rank * world * E;
+    for (int i = threadIdx.x; i < world * E; i += blockDim.x) dst[i] = cnt[i];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, seq);
+}
+
+__global__ void k_dest_to_i64(int64_t m, const int32_t* __restrict__ d, int64_t* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < m) out[i] = d[i];
+}
+
+// Receive layout + send offsets from the exchanged counts C[s][d][e].
+__global__ void __launch_bounds__(256) k_layout(int world, int rank, int E,
+                                                const int32_t* __restrict__ owners,
+                                                const int32_t* __restrict__ nrep,
+                                                const int32_t* __restrict__ cnt_in,
+                                                const uint32_t* __restrict__ flags,
+                                                int64_t* __restrict__ recv_per_layer,
+                                                int64_t cap_rows, Layout* __restrict__ lay,
+                                                uint32_t seq, WaitCfg wc) {
+  __shared__ int R[kMaxWorld][kMaxExperts];       // rows per (dest, expert)
+  __shared__ int before[kMaxWorld][kMaxExperts];  // rows from sources < rank
+  __shared__ int seg[kMaxWorld][kMaxExperts];
+  __shared__ unsigned char res[kMaxWorld][kMaxExperts];
+  __shared__ int overflow[kMaxWorld];
+  if (threadIdx.x < world) wait_flag(flags + threadIdx.x, seq, kErrWaitCounts, wc);
+  __syncthreads();
+  for (int i = threadIdx.x; i < world * E; i += blockDim.x) {
+    const int d = i / E, e = i % E;
+    int tot = 0, bef = 0;
+    for (int s = 0; s < world; ++s) {
+      const int c = cnt_in[((int64_t)s * world + d) * E + e];
+      tot += c;
+      if (s < rank) bef += c;
+    }
+    R[d][e] = tot;
+    before[d][e] = bef;
+    unsigned char r = 0;
+    for (int j = 0; j < nrep[e]; ++j) r |= owners[e * kMaxWorld + j] == d;
+    res[d][e] = r;
+    if (tot > 0 && !r) set_err(wc.err, kErrNotResident);
+  }
+  __syncthreads();
+  if (threadIdx.x < world) {
+    const int d = threadIdx.x;
+    int64_t b = 0;
+    for (int e = 0; e < E; ++e) {
+      seg[d][e] = (int)b;
+      if (res[d][e]) b += (R[d][e] + kRowAlign - 1) / kRowAlign * kRowAlign;
+    }
+    overflow[d] = b > cap_rows;
+    if (b > cap_rows) set_err(wc.err, kErrCapacity);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < world * E; i += blockDim.x) {
+    const int d = i / E, e = i % E;
+    lay->dst_off[d * kMaxExperts + e] = overflow[d] ? -1 : seg[d][e] + before[d][e];
+  }
+  if (threadIdx.x == 0) {
+    int j = 0, tiles = 0, rows = 0, end = 0;
+    for (int e = 0; e < E; ++e) {
+      if (!res[rank][e]) continue;
+      lay->local_expert[j] = e;
+      lay->seg_base[j] = seg[rank][e];
+      lay->seg_rows[j] = R[rank][e];
+      lay->tile_prefix[j] = tiles;
+      const int t = (R[rank][e] + kRowAlign - 1) / kRowAlign;
+      tiles += t;
+      rows += R[rank][e];
+      end = seg[rank][e] + t * kRowAlign;
+      ++j;
+    }
+    lay->tile_prefix[j] = tiles;
+    lay->n_local = j;
+    lay->total_mtiles = overflow[rank] ? 0 : tiles;
+    lay->total_rows = end;
+    lay->recv_rows = rows;
+    if (recv_per_layer) recv_per_layer[0] += rows;
+  }
+}
+
+}  // namespace
+
+void launch_route(int64_t n, int topk, int experts, int world, int rank,
+                  const int64_t* topk_idx, const uint8_t* valid, const int32_t* owners_l,
+                  const int32_t* nrep_l, int64_t* rr_l, int64_t* route_counts_l,
+                  int32_t* chunk_hist, int32_t* ent_dest, int32_t* ent_grp, int32_t* my_counts,
+                  const PeerPtrs& peers, uint32_t seq, WaitCfg wc, cudaStream_t st) {
+  const int nchunks = (int)((n + kRouteChunkTokens - 1) / kRouteChunkTokens);
+  if (nchunks > 0) {
+    k_route_hist<<<nchunks, kRouteThreads, 0, st>>>(n, topk, experts, topk_idx, valid, chunk_hist,
+                                                    wc.err);
+    k_route_rank<<<nchunks, kRouteThreads, 0, st>>>(n, topk, experts, topk_idx, valid, owners_l,
+                                                    nrep_l, rr_l, chunk_hist, ent_dest, ent_grp);
+  }
+  k_route_finalize<<<1, 256, 0, st>>>(nchunks, experts, world, rank, owners_l, nrep_l, rr_l,
+                                      route_counts_l, chunk_hist, my_counts, peers, seq, 1);
+}
+
+void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids, const int32_t* owners_l,
+                      const int32_t* nrep_l, int64_t* rr_l, int32_t* chunk_hist,
+                      int32_t* ent_dest, int32_t* ent_grp, int32_t* my_counts, int64_t* dest_out,
+                      WaitCfg wc, cudaStream_t st) {
+  const int nchunks = (int)((m + kRouteChunkTokens - 1) / kRouteChunkTokens);
+  if (nchunks > 0) {
+    k_route_hist<<<nchunks, kRouteThreads, 0, st>>>(m, 1, experts, expert_ids, nullptr, chunk_hist,
+                                                    wc.err);
+    k_route_rank<<<nchunks, kRouteThreads, 0, st>>>(m, 1, experts, expert_ids, nullptr, owners_l,
+                                                    nrep_l, rr_l, chunk_hist, ent_dest, ent_grp);
+    k_dest_to_i64<<<(unsigned)((m + 255) / 256), 256, 0, st>>>(m, ent_dest, dest_out);
+  }
+  PeerPtrs none{};
+  k_route_finalize<<<1, 256, 0, st>>>(nchunks, experts, kMaxWorld, 0, owners_l, nrep_l, rr_l,
+                                      nullptr, chunk_hist, my_counts, none, 0, 0);
+}
+
+void launch_layout(int world, int rank, int experts, const int32_t* owners_l,
+                   const int32_t* nrep_l, const int32_t* cnt_in_local, const uint32_t* flags_local,
+                   int64_t* recv_per_layer_l, int64_t cap_rows, Layout* layout, uint32_t seq,
+                   WaitCfg wc, cudaStream_t st) {
+  k_layout<<<1, 256, 0, st>>>(world, rank, experts, owners_l, nrep_l, cnt_in_local, flags_local,
+                              recv_per_layer_l, cap_rows, layout, seq, wc);
+}
+
+}  // namespace mep
