@@ -1,0 +1,394 @@
+"""MoE-layer throughput on B200: one expert-parallel GraniteMoE-shaped layer step
+(router + route + dispatch + grouped SwiGLU experts + combine + residual).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workload (shape (a)): hidden 1024, 32 experts, top-8,
+intermediate 512, bf16, Zipf(1.2)-skewed router (layer-0 bias), 16384 tokens
+per step in total, split evenly over the ranks (strong scaling), balanced
+replica plan (2 slots per rank) from a naive profiling pass when N > 1.
+Seeded synthetic tensors stand in for the checkpoint and prompts.
+
+Prints one JSON line (rank 0). `value` is whole-job tokens/s of the device
+step (inputs resident in HBM, L2 flushed between steps, per-step CUDA events,
+max over ranks); `e2e` is the same metric through the public API with the
+step's inputs copied from pinned host memory and its output copied back
+inside the timed region. `--impl reference` times the CPU checker's
+restatement of the reference's LocalMoEBackend + router on this host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT / "mini-ep_b200", ROOT):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+import torch  # noqa: E402
+
+METRIC = "MoE layer tokens/s"
+UNIT = "tokens/s"
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_BF16_TFLOPS = 1590.0
+KERNELS_PER_STEP = 10  # router, hist, rank, finalize, layout, dispatch, wait, gemm1, gemm2, combine
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--shape", choices=["a", "b"], default="a")
+    ap.add_argument("--tokens", type=int, default=16384, help="tokens per step, all ranks")
+    ap.add_argument("--plan", choices=["naive", "balanced"], default="balanced")
+    ap.add_argument("--cpu-sample", type=int, default=2048, help="tokens per CPU sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--force-simt", action="store_true")
+    return ap.parse_args()
+
+
+def workload_name(a) -> str:
+    return f"moe_layer_shape_{a.shape}_{a.tokens}tok_zipf1.2_{a.plan}"
+
+
+def config(a, sh) -> dict:
+    return {"workload": workload_name(a), "tokens_per_step": a.tokens, "hidden": sh["hidden"],
+            "experts": sh["experts"], "topk": sh["topk"], "inter": sh["inter"],
+            "router": "zipf(1.2) bias x2.0, layer 0", "placement": a.plan,
+            "l2": "flushed between timed steps (512 MiB write, outside the step events)"}
+
+
+# ------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of this GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        time.sleep(0.05)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# --------------------------------------------------------------- CPU legs
+def cpu_sample_inputs(sh, n_tokens, seed=0):
+    from miniep_b200 import synth
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n_tokens, seed=seed,
+                          dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0]
+    h = synth.make_tokens(n_tokens, sh["hidden"], seed=seed + 7, dtype=torch.bfloat16)
+    return lb, bias, h
+
+
+def cpu_step(oracle, lb, bias, h, k):
+    from miniep_b200 import synth
+    out, _, _ = oracle.moe_block(h, lb.x, lb.router, lb.w_in, lb.w_out, k,
+                                 synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
+    return out
+
+
+def cpu_baseline(sh, sample_tokens, min_seconds=10.0, max_reps=20) -> dict:
+    """The CPU checker's restatement of the reference path (router +
+    LocalMoEBackend + residual) on this host's cores, on a bounded sample."""
+    from oracle import moe_oracle
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    lb, bias, h = cpu_sample_inputs(sh, sample_tokens)
+    cpu_step(moe_oracle, lb, bias, h, sh["topk"])  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while reps < max_reps:
+        cpu_step(moe_oracle, lb, bias, h, sh["topk"])
+        reps += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": reps * sample_tokens / dt, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{reps} x {sample_tokens} tokens of the same workload (bf16, shape, "
+                      f"Zipf router) through oracle.moe_block, {dt:.1f} s"}
+
+
+def run_reference(a):
+    """--impl reference: the CPU path of the reference, timed on host cores."""
+    from miniep_b200 import synth
+    from oracle import moe_oracle
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sh = synth.SHAPES[a.shape]
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    sample = min(a.cpu_sample, a.tokens)
+    lb, bias, h = cpu_sample_inputs(sh, sample)
+    for _ in range(a.warmup):
+        cpu_step(moe_oracle, lb, bias, h, sh["topk"])
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        cpu_step(moe_oracle, lb, bias, h, sh["topk"])
+    dt = time.perf_counter() - t0
+    value = a.steps * sample / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": dt / a.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": config(a, sh),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{sample} tokens per step through oracle.moe_block "
+                                   f"(router + LocalMoEBackend + residual restated in torch CPU)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU leg
+def main_b200(a):
+    import torch.distributed as dist
+    from miniep_b200 import Comm, EPMoEBackend, Placement, _lib, plan_balanced, synth
+    from miniep_b200.ep import router_topk
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=dev)
+    sh = synth.SHAPES[a.shape]
+    H, E, k, I = sh["hidden"], sh["experts"], sh["topk"], sh["inter"]
+    start, stop = synth.split_tokens(a.tokens, world, rank)
+    n = stop - start
+    # same weights on every rank (same seed), each rank its own token shard
+    lt = synth.make_layer(H, E, I, a.tokens, seed=0, dtype=torch.bfloat16, device=dev)
+    bias = synth.zipf_router_bias(1, E)[0].to(dev)
+    x = lt.x[start:stop].contiguous()
+    h = synth.make_tokens(a.tokens, H, seed=7, dtype=torch.bfloat16, device=dev)[start:stop].contiguous()
+    rm = synth.GRANITE_RESIDUAL_MULTIPLIER
+
+    comm = Comm(num_layers=1, num_experts=E, topk=k, hidden=H, inter=I, max_tokens=n,
+                dtype=torch.bfloat16, device=local, timeout_ms=20000)
+    if a.force_simt:
+        comm.set_option("force_simt", 1)
+    placement = Placement.naive(1, E, world)
+    if world > 1 and a.plan == "balanced":
+        comm.install(placement)
+        idx, _ = router_topk(comm, x, lt.router, bias)
+        counts = torch.bincount(idx.reshape(-1), minlength=E).to(torch.int64)
+        dist.all_reduce(counts)
+        placement, _ = plan_balanced(counts.view(1, E).cpu(), world, slots_per_rank=2)
+    comm.install(placement)
+    mine = placement.experts_of_rank(rank)[0]
+    w_in, w_out = lt.w_in[mine].contiguous(), lt.w_out[mine].contiguous()
+    lt_router = lt.router.contiguous()
+    del lt
+    be = EPMoEBackend(0, comm, placement, mine, w_in, w_out, None)
+
+    L, ctx = _lib.lib(), comm._ctx
+    idx = torch.empty(n, k, dtype=torch.int64, device=dev)
+    gate = torch.empty(n, k, dtype=torch.bfloat16, device=dev)
+    h_out = torch.empty_like(h)
+    P = _lib.ptr
+
+    def step(st, ev_ffn=None):
+        # exactly mep_moe_block's sequence, with events around the expert FFN stage
+        _lib.check(L.mep_router_topk(ctx, P(x), P(lt_router), P(bias), n, P(idx), P(gate),
+                                     None, st), ctx)
+        _lib.check(L.mep_route(ctx, 0, P(idx), None, n, len(mine), st), ctx)
+        _lib.check(L.mep_dispatch(ctx, P(x), P(idx), n, st), ctx)
+        if ev_ffn:
+            ev_ffn[0].record()
+        _lib.check(L.mep_expert_ffn(ctx, P(w_in), P(w_out), len(mine), st), ctx)
+        if ev_ffn:
+            ev_ffn[1].record()
+        _lib.check(L.mep_combine(ctx, P(gate), None, n, P(h), rm, None, P(h_out), st), ctx)
+
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(a.warmup):
+        step(st)
+    torch.cuda.synchronize()
+    comm.check()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps)]
+    ffn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(a.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for i in range(a.steps):
+        flush.zero_()
+        if world > 1:
+            dist.barrier()
+        starts[i].record()
+        step(st, ffn[i])
+        ends[i].record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    wall = time.perf_counter() - wall0
+    comm.check()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ffn_ms = [s.elapsed_time(e) for s, e in ffn]
+    t_step = torch.tensor([sum(step_ms) / a.steps, sum(ffn_ms) / a.steps], device=dev,
+                          dtype=torch.float64)
+    recv_rows = comm.last_recv_rows()
+    rows_t = torch.tensor([recv_rows], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t_step, op=dist.ReduceOp.MAX)
+    ms_step, ms_ffn = t_step.tolist()
+
+    # e2e: the public API with host buffers, copies inside the timed region
+    e2e = None
+    if not a.no_e2e:
+        x_host = x.cpu().pin_memory()
+        h_host = h.cpu().pin_memory()
+        out_host = torch.empty_like(h_host).pin_memory()
+        xd, hd = torch.empty_like(x), torch.empty_like(h)
+        rw = lt_router
+
+        def e2e_step():
+            xd.copy_(x_host, non_blocking=True)
+            hd.copy_(h_host, non_blocking=True)
+            ho, _, _ = be.moe_block(hd, xd, rw, rm, bias=bias)
+            out_host.copy_(ho, non_blocking=True)
+
+        for _ in range(max(1, a.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": a.tokens / (te.item() / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": (x_host.numel() + h_host.numel()) * 2,
+               "d2h_bytes_per_step": out_host.numel() * 2,
+               "ms_per_step": te.item(), "path": "EPMoEBackend.moe_block"}
+        comm.check()
+    clk = clocks.stop()
+
+    if world > 1:
+        dist.all_reduce(rows_t)
+    total_rows = rows_t.item()
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(sh, a.cpu_sample)
+
+    if rank == 0:
+        peaks = json.loads(PEAKS_FILE.read_text()) if PEAKS_FILE.exists() else {}
+        peak = peaks.get("bf16_tflops_sustained")
+        peak_src = "measured sustained bf16 (MEASURED_PEAKS.json)"
+        if peak is None:
+            peak, peak_src = FALLBACK_BF16_TFLOPS, "fallback"
+        flops_rank0 = recv_rows * 6.0 * H * I  # algorithmic FLOPs of this rank's FFN launch
+        achieved = flops_rank0 / (sum(ffn_ms) / a.steps / 1e3) / 1e12
+        line = {
+            "metric": METRIC, "value": a.tokens / (ms_step / 1e3), "unit": UNIT,
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random weights/tokens, Zipf-skewed router)",
+            "config": dict(config(a, sh), parallelism=f"ep{world}"),
+            "roofline": {"bound": "tensor", "kernel": "expert FFN stage (tcgen05 GEMM1+SwiGLU, "
+                                                      "GEMM2+return stores), rank 0",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_source": peak_src,
+                         "flops_per_launch": flops_rank0, "ms_per_launch": sum(ffn_ms) / a.steps,
+                         "traffic": None},
+            "ffn_ms_per_step_max_rank": ms_ffn,
+            "layer_roofline_frac": (a.tokens * (6.0 * k * H * I + 2.0 * H * E) / world
+                                    / (ms_step / 1e3) / 1e12) / peak,
+            "recv_rows_total": total_rows,
+            "wall_s_timed_region": wall,
+            "gpu_launches": KERNELS_PER_STEP * a.steps,
+            "clocks": clk,
+        }
+        if e2e:
+            line["e2e"] = e2e
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    comm.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+        return
+    main_b200(a)
+
+
+if __name__ == "__main__":
+    main()

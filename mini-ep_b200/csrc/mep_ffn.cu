@@ -420,7 +420,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
       const int b = it & 1;
       const uint32_t aph = (uint32_t)(it >> 1) & 1u;
-      if (!mbar_wait(&S->tfull[b], aph, S, args.err)) break;
+      // one lane waits, the warp follows its verdict: the TMEM loads below are
+      // warp-collective, so the warp must never split on a timeout
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&S->tfull[b], aph, S, args.err);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
       fence_after();
       const TileCoord c =
           decode_tile(t, args.ntiles_n, 1, BM, S->n_local, S->prefix, S->base, S->rows);

@@ -1,0 +1,299 @@
+"""CUDA path vs the CPU checker and the reference's fixtures, through the C ABI.
+
+Bars: routing indices and every count bit-exact (away from exact logit ties,
+where the CUDA router's rule is "lower expert index first" and is checked
+against its own logits); layer outputs within 1e-5 relative (fp32) and
+within 2e-2 max-abs of an fp32 reference (bf16).
+"""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import RawCtx, require_gpu, stream, world1_backend, world1_comm
+from miniep_b200 import MEPError, synth
+from miniep_b200.ep import router_topk
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+FP32_RTOL = 1e-5       # fp32 outputs: max|gpu - ref| <= 1e-5 * max|ref|
+BF16_ATOL = 2e-2       # bf16 outputs vs an fp32 reference, max-abs
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    require_gpu()
+
+
+def _bf16(bits):
+    return torch.from_numpy(bits.astype(np.int16)).view(torch.bfloat16)
+
+
+def _fp32_ref(x, idx, gate, w_in, w_out, valid=None):
+    return O.local_moe(x.float().cpu(), idx.cpu(), gate.float().cpu(), w_in.float().cpu(),
+                       w_out.float().cpu(), None if valid is None else valid.cpu())
+
+
+# ----------------------------------------------------------------- router
+def test_router_fp32_config1(golden):
+    g = np.load(golden / "router_local_fp32.npz")
+    sh = synth.SHAPES["a"]
+    lt = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], 512, seed=0)
+    be = world1_backend(lt.w_in, lt.w_out, sh["topk"], 512)
+    idx, gate, logits = router_topk(be.comm, lt.x.cuda(), lt.router.cuda(), return_logits=True)
+    ref_logits = torch.from_numpy(g["logits"])
+    assert torch.allclose(logits.cpu(), ref_logits, rtol=1e-5, atol=1e-6)
+    srt = ref_logits.sort(dim=-1, descending=True).values[:, : sh["topk"] + 1]
+    stable = ((srt[:, :-1] - srt[:, 1:]) > 1e-4 * srt.abs().max()).all(dim=-1)
+    assert stable.float().mean() > 0.9
+    ref_idx = torch.from_numpy(g["topk_idx"]).long()
+    assert torch.equal(idx.cpu()[stable], ref_idx[stable])
+    assert torch.allclose(gate.cpu()[stable], torch.from_numpy(g["topk_gate"])[stable],
+                          rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("shape,n", [("a", 4096), ("b", 1024)])
+def test_router_bf16_skewed(shape, n):
+    sh = synth.SHAPES[shape]
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=1, dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0]
+    comm = world1_comm(sh["experts"], sh["topk"], sh["hidden"], sh["inter"], n, torch.bfloat16)
+    idx, gate, logits = router_topk(comm, lb.x.cuda(), lb.router.cuda(), bias.cuda(),
+                                    return_logits=True)
+    idx, gate, logits = idx.cpu(), gate.cpu(), logits.cpu()
+    ref_idx, ref_gate, ref_logits = O.router_topk(lb.x, lb.router, sh["topk"], bias)
+    # logits: fp32 accumulation in another order, then the same rounding
+    ulp = ref_logits.float().abs().clamp_min(2.0 ** -20) * 2.0 ** -7
+    assert torch.all((logits - ref_logits.float()).abs() <= ulp)
+    same_row = (logits == ref_logits.float()).all(dim=1)
+    assert same_row.float().mean() > 0.9
+    # selection rule is exact on the kernel's own logits (lower index first on ties)
+    assert torch.equal(idx, O.topk_lowest_index(logits, sh["topk"]))
+    # against the reference: bit-exact wherever the logits agree and hold no tie
+    ok = same_row & ~O.boundary_ties(ref_logits, sh["topk"])
+    assert torch.equal(idx[ok], ref_idx[ok])
+    assert torch.equal(logits.gather(1, idx)[same_row],
+                       ref_logits.float().gather(1, ref_idx)[same_row])
+    assert (gate.float() - ref_gate.float()).abs()[ok].max() <= 2.0 ** -8
+    # per-expert histogram of the kernel's routing == the reference's on tie-free rows
+    assert torch.equal(torch.bincount(idx[ok].reshape(-1), minlength=sh["experts"]),
+                       torch.bincount(ref_idx[ok].reshape(-1), minlength=sh["experts"]))
+
+
+# ---------------------------------------------------------------- dest ranks
+def test_dest_ranks_matches_reference_round_robin(golden):
+    g = np.load(golden / "dest_ranks.npz")
+    plan = json.loads(str(g["plan"]))
+    owners = O.owners_from_plan(plan)
+    L, E = len(owners), len(owners[0])
+    raw = RawCtx(0, 4, L, E, 8, 1024, 512, 64, torch.bfloat16)
+    try:
+        for l in range(L):
+            table, n_rep = O.build_table(owners[l])
+            raw.call("mep_set_placement", l, table.ctypes.data, n_rep.ctypes.data, table.shape[1])
+        raw.call("mep_reset_rr", stream())
+        for l in range(L):
+            for call in range(3):
+                ids = torch.from_numpy(g[f"l{l}_c{call}_ids"].astype(np.int64)).cuda()
+                out = torch.empty_like(ids)
+                raw.call("mep_dest_ranks", l, ids.data_ptr(), ids.numel(), out.data_ptr(), stream())
+                want = torch.from_numpy(g[f"l{l}_c{call}_dest"].astype(np.int64))
+                assert torch.equal(out.cpu(), want), (l, call)
+        # reset_rr restarts the round robin
+        raw.call("mep_reset_rr", stream())
+        ids = torch.from_numpy(g["l0_c0_ids"].astype(np.int64)).cuda()
+        out = torch.empty_like(ids)
+        raw.call("mep_dest_ranks", 0, ids.data_ptr(), ids.numel(), out.data_ptr(), stream())
+        assert torch.equal(out.cpu(), torch.from_numpy(g["l0_c0_dest"].astype(np.int64)))
+        torch.cuda.synchronize()
+        raw.call("mep_check")
+    finally:
+        raw.close()
+
+
+# ---------------------------------------------------------------- layer
+def test_layer_fp32_config1_matches_reference(golden):
+    g = np.load(golden / "router_local_fp32.npz")
+    sh = synth.SHAPES["a"]
+    lt = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], 512, seed=0)
+    idx = torch.from_numpy(g["topk_idx"]).long()
+    gate = torch.from_numpy(g["topk_gate"])
+    valid = torch.from_numpy(g["valid"])
+    be = world1_backend(lt.w_in, lt.w_out, sh["topk"], 512)
+    out = be(lt.x.cuda(), idx.cuda(), gate.cuda()).cpu()
+    head = torch.from_numpy(g["out_head"])
+    tol = FP32_RTOL * head.abs().max()
+    assert (out[:48] - head).abs().max() <= tol
+    full = O.local_moe(lt.x, idx, gate, lt.w_in, lt.w_out)
+    assert (out - full).abs().max() <= FP32_RTOL * full.abs().max()
+    outm = be(lt.x.cuda(), idx.cuda(), gate.cuda(), valid_mask=valid.cuda()).cpu()
+    assert (outm[:48] - torch.from_numpy(g["outm_head"])).abs().max() <= tol
+    assert torch.all(outm[~valid] == 0)
+    snap = be.stats.snapshot()
+    kept = int(valid.sum()) * sh["topk"]
+    assert snap["recv_tokens"] == 512 * sh["topk"] + kept
+    want = torch.bincount(idx.reshape(-1), minlength=sh["experts"]) + \
+        torch.bincount(idx[valid].reshape(-1), minlength=sh["experts"])
+    assert snap["route_counts"] == [want.tolist()]
+    be.comm.check()
+
+
+@pytest.mark.parametrize("force_simt", [False, True], ids=["tcgen05", "cuda_cores"])
+@pytest.mark.parametrize("n", [1, 127, 300, 2048])
+def test_layer_bf16_shape_a(n, force_simt):
+    sh = synth.SHAPES["a"]
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=2, dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0]
+    idx, gate, _ = O.router_topk(lb.x, lb.router, sh["topk"], bias)
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], max(n, 256), force_simt=force_simt)
+    out = be(lb.x.cuda(), idx.cuda(), gate.cuda()).cpu()
+    ref32 = _fp32_ref(lb.x, idx, gate, lb.w_in, lb.w_out)
+    assert (out.float() - ref32).abs().max() <= BF16_ATOL
+    ref16 = O.local_moe(lb.x, idx, gate, lb.w_in, lb.w_out)
+    # against the bf16 reference itself: same roundings, so nearly all equal
+    d = (out.float() - ref16.float()).abs()
+    assert d.max() <= 2e-2 and (d == 0).float().mean() > 0.8
+    be.comm.check()
+
+
+def test_tcgen05_and_cuda_core_paths_agree():
+    sh = synth.SHAPES["a"]
+    n = 4096
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=4, dtype=torch.bfloat16)
+    idx, gate, _ = O.router_topk(lb.x, lb.router, sh["topk"], synth.zipf_router_bias(1, 32)[0])
+    a = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
+    b = world1_backend(lb.w_in, lb.w_out, sh["topk"], n, force_simt=True)
+    xa, ia, ga = lb.x.cuda(), idx.cuda(), gate.cuda()
+    oa, ob = a(xa, ia, ga), b(xa, ia, ga)
+    d = (oa.float() - ob.float()).abs()
+    assert d.max() <= 1e-2 and (d == 0).float().mean() > 0.9
+    a.comm.check()
+    b.comm.check()
+
+
+def test_layer_bf16_shape_b():
+    sh = synth.SHAPES["b"]
+    n = 384
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=5, dtype=torch.bfloat16)
+    idx, gate, _ = O.router_topk(lb.x, lb.router, sh["topk"], synth.zipf_router_bias(1, 64)[0])
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
+    out = be(lb.x.cuda(), idx.cuda(), gate.cuda()).cpu()
+    ref32 = _fp32_ref(lb.x, idx, gate, lb.w_in, lb.w_out)
+    assert (out.float() - ref32).abs().max() <= BF16_ATOL
+    be.comm.check()
+
+
+def test_moe_block_matches_reference_block(golden):
+    g = np.load(golden / "router_local_bf16.npz")
+    sh = synth.SHAPES["a"]
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], 128, seed=0,
+                          dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0]
+    h = synth.make_tokens(128, sh["hidden"], seed=7, dtype=torch.bfloat16)
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], 128)
+    h_out, idx, gate = be.moe_block(h.cuda(), lb.x.cuda(), lb.router.cuda(),
+                                    synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias.cuda())
+    ref_idx = torch.from_numpy(g["topk_idx"]).long()
+    same = (idx.cpu().sort(1).values == ref_idx.sort(1).values).all(dim=1)
+    assert same.float().mean() > 0.5  # the rest differ only by the order of exact ties
+    d = (h_out.cpu().float() - _bf16(g["block_out"]).float()).abs()
+    assert d[same].max() <= BF16_ATOL
+    # rows with a different tie pick still equal h + rm * moe(x) of their own routing
+    ref = O.residual_add(h, O.local_moe(lb.x, idx.cpu(), gate.cpu(), lb.w_in, lb.w_out),
+                         synth.GRANITE_RESIDUAL_MULTIPLIER)
+    assert (h_out.cpu().float() - ref.float()).abs().max() <= BF16_ATOL
+    be.comm.check()
+
+
+# ------------------------------------------------------------- edge cases
+def test_empty_masked_and_single_hot_expert():
+    sh = synth.SHAPES["a"]
+    n = 640
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=6, dtype=torch.bfloat16)
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
+    x = lb.x.cuda()
+    # n = 0: the step still runs (lockstep) and returns an empty tensor
+    out0 = be(x[:0], torch.zeros(0, 8, dtype=torch.long, device="cuda"),
+              torch.zeros(0, 8, dtype=torch.bfloat16, device="cuda"))
+    assert out0.shape == (0, sh["hidden"])
+    # every token masked: zeros, no expert rows received
+    idx = torch.stack([torch.randperm(32)[:8] for _ in range(n)])
+    gate = torch.full((n, 8), 0.125, dtype=torch.bfloat16)
+    outm = be(x, idx.cuda(), gate.cuda(), valid_mask=torch.zeros(n, dtype=torch.bool, device="cuda"))
+    assert torch.all(outm == 0)
+    assert be.comm.last_recv_rows() == 0
+    # one expert in every token's first slot: a 640-row segment (5 tiles)
+    idx[:, 0] = 31
+    idx[:, 1:] = torch.stack([torch.randperm(31)[:7] for _ in range(n)])
+    out = be(x, idx.cuda(), gate.cuda()).cpu()
+    ref32 = _fp32_ref(lb.x, idx, gate, lb.w_in, lb.w_out)
+    assert (out.float() - ref32).abs().max() <= BF16_ATOL
+    assert be.comm.last_recv_rows() == n * 8
+    be.comm.check()
+
+
+def test_full_size_workload_properties():
+    """BASELINE shape (a) at 16K tokens: counts exact, sampled rows vs the checker."""
+    sh = synth.SHAPES["a"]
+    n = 16384
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=0, dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0]
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
+    x = lb.x.cuda()
+    idx, gate = router_topk(be.comm, x, lb.router.cuda(), bias.cuda())
+    out = be(x, idx, gate)
+    out2 = be(x, idx, gate)
+    assert torch.equal(out, out2)  # deterministic, no atomics
+    snap = be.stats.snapshot()
+    cnt = torch.bincount(idx.reshape(-1).cpu(), minlength=sh["experts"])
+    assert snap["route_counts"][0] == (2 * cnt).tolist()
+    assert snap["recv_tokens"] == 2 * n * sh["topk"]
+    assert int(cnt.max()) > 2 * int(cnt.float().mean())  # skewed, as configured
+    rows = torch.randperm(n, generator=torch.Generator().manual_seed(0))[:192]
+    ref32 = _fp32_ref(lb.x[rows], idx.cpu()[rows], gate.cpu()[rows], lb.w_in, lb.w_out)
+    assert (out.cpu()[rows].float() - ref32).abs().max() <= BF16_ATOL
+    assert torch.isfinite(out.float()).all()
+    be.comm.check()
+
+
+def test_device_errors_are_reported_and_recoverable():
+    sh = synth.SHAPES["a"]
+    n = 64
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=8, dtype=torch.bfloat16)
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
+    x = lb.x.cuda()
+    idx = torch.stack([torch.randperm(32)[:8] for _ in range(n)])
+    gate = torch.full((n, 8), 0.125, dtype=torch.bfloat16)
+    bad = idx.clone()
+    bad[3, 2] = 99
+    be(x, bad.cuda(), gate.cuda())
+    with pytest.raises(MEPError, match="outside"):
+        be.comm.check()
+    # a wait that nothing satisfies ends with an error instead of hanging
+    from miniep_b200 import _lib
+    _lib.check(_lib.lib().mep_debug_wait(be.comm._ctx, 0x7fffffff, 200, stream()), be.comm._ctx)
+    with pytest.raises(MEPError, match="debug wait"):
+        be.comm.check()
+    # the context keeps working
+    out = be(x, idx.cuda(), gate.cuda()).cpu()
+    ref32 = _fp32_ref(lb.x, idx, gate, lb.w_in, lb.w_out)
+    assert (out.float() - ref32).abs().max() <= BF16_ATOL
+    be.comm.check()
+
+
+def test_argument_errors():
+    sh = synth.SHAPES["a"]
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], 8, seed=8, dtype=torch.bfloat16)
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], 8)
+    idx = torch.zeros(16, 8, dtype=torch.long, device="cuda")
+    with pytest.raises(MEPError, match="max_tokens"):
+        be(torch.zeros(16, 1024, dtype=torch.bfloat16, device="cuda"), idx,
+           torch.zeros(16, 8, dtype=torch.bfloat16, device="cuda"))
+    with pytest.raises(MEPError, match="CUDA"):
+        be(torch.zeros(8, 1024, dtype=torch.float32, device="cuda"), idx[:8],
+           torch.zeros(8, 8, dtype=torch.bfloat16, device="cuda"))
+    be.local_experts = [0, 1]
+    with pytest.raises(MEPError, match="local_experts"):
+        be(lb.x.cuda(), idx[:8], torch.zeros(8, 8, dtype=torch.bfloat16, device="cuda"))
