@@ -19,7 +19,14 @@ from oracle import moe_oracle as O
 pytestmark = pytest.mark.gpu
 
 FP32_RTOL = 1e-5       # fp32 outputs: max|gpu - ref| <= 1e-5 * max|ref|
-BF16_ATOL = 2e-2       # bf16 outputs vs an fp32 reference, max-abs
+BF16_ATOL = 2e-2       # bf16 outputs vs an fp32 reference, max-abs, for outputs of unit scale
+
+
+def bf16_tol(ref32):
+    """2e-2 max-abs, scaled by the output magnitude when it exceeds 1: shape
+    (b) outputs reach |3.6| and the reference's own bf16 path is already
+    2.8e-2 away from fp32 there (one bf16 ulp at 2..4 is 1.6e-2)."""
+    return BF16_ATOL * max(1.0, float(ref32.abs().max()))
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -44,7 +51,8 @@ def test_router_fp32_config1(golden):
     be = world1_backend(lt.w_in, lt.w_out, sh["topk"], 512)
     idx, gate, logits = router_topk(be.comm, lt.x.cuda(), lt.router.cuda(), return_logits=True)
     ref_logits = torch.from_numpy(g["logits"])
-    assert torch.allclose(logits.cpu(), ref_logits, rtol=1e-5, atol=1e-6)
+    # 1e-5 relative to the logit scale (fp32 sums of 1024 products in another order)
+    assert (logits.cpu() - ref_logits).abs().max() <= FP32_RTOL * ref_logits.abs().max()
     srt = ref_logits.sort(dim=-1, descending=True).values[:, : sh["topk"] + 1]
     stable = ((srt[:, :-1] - srt[:, 1:]) > 1e-4 * srt.abs().max()).all(dim=-1)
     assert stable.float().mean() > 0.9
@@ -181,7 +189,10 @@ def test_layer_bf16_shape_b():
     be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
     out = be(lb.x.cuda(), idx.cuda(), gate.cuda()).cpu()
     ref32 = _fp32_ref(lb.x, idx, gate, lb.w_in, lb.w_out)
-    assert (out.float() - ref32).abs().max() <= BF16_ATOL
+    assert (out.float() - ref32).abs().max() <= bf16_tol(ref32)
+    # and no further from fp32 than the reference's own bf16 path, within one ulp
+    ref16 = O.local_moe(lb.x, idx, gate, lb.w_in, lb.w_out)
+    assert (out.float() - ref16.float()).abs().max() <= 2.0 ** -6 * max(1.0, float(ref32.abs().max()))
     be.comm.check()
 
 
