@@ -47,7 +47,8 @@ typedef struct mep_ctx mep_ctx;
 /* Library version (major*10000 + minor*100 + patch). */
 int mep_version(void);
 
-/* Message for the last failed call on `ctx` (or of mep_ctx_create when ctx is NULL). */
+/* Message for the last failed call on `ctx`; with ctx NULL, of the last failed
+ * call that takes no context (mep_ctx_create, mep_dest_ranks_noalloc). */
 const char* mep_last_error(const mep_ctx* ctx);
 
 /*
@@ -189,6 +190,31 @@ int mep_set_option(mep_ctx* ctx, const char* name, int64_t value);
  * device error and returns, so the context stays usable.
  */
 int mep_debug_wait(mep_ctx* ctx, uint32_t target, int64_t timeout_ms, void* stream);
+
+/*
+ * mep_dest_ranks without a context and without any device allocation.
+ * This entry point has no counterpart in the reference. It exists for callers
+ * that cannot call cudaMalloc: a serving process that has handed all free HBM
+ * to its own memory pool (a later cudaMalloc fails or fragments that pool),
+ * or host code on a latency-critical path, where cudaMalloc/cudaFree would
+ * synchronise the device. Results equal mep_dest_ranks for the same table,
+ * round-robin state and ids.
+ *   table (host, E x rmax int64) / n_rep (host, E int64): one layer's
+ *     placement, as for mep_set_placement; world: ranks in the placement;
+ *   rr (device, E int64): round-robin state of that layer, updated in place
+ *     (zero it to reset, like Placement.reset_rr);
+ *   expert_ids / dest_out (device, m int64), m <= 65536.
+ * Its intermediate buffers live in one fixed array of about 650 KiB that
+ * every GPU loading this library keeps until the process exits. All calls
+ * share that array: calls whose kernels can overlap on one GPU race, so the
+ * caller must serialise them. The first call on each device looks up the
+ * array's device address; make it before any stream capture. Larger calls
+ * fail with MEP_ERR_INVALID; messages come from mep_last_error(NULL).
+ */
+int mep_dest_ranks_noalloc(int num_experts, int world, const int64_t* table,
+                           const int64_t* n_rep, int rmax, int64_t* rr,
+                           const int64_t* expert_ids, int64_t m, int64_t* dest_out,
+                           void* stream);
 
 #ifdef __cplusplus
 }

@@ -114,6 +114,11 @@ const int32_t* nrep_of(const mep_ctx* c, int layer) { return c->nrep + (int64_t)
 
 }  // namespace
 
+namespace mep {
+// Message for mep_last_error(NULL), set by entry points that take no context.
+void set_global_error(const std::string& msg) { g_create_err = msg; }
+}  // namespace mep
+
 extern "C" {
 
 int mep_version(void) { return 100; }
