@@ -181,7 +181,11 @@ struct Smem {
   int n_local, total;
   int prefix[kMaxExperts + 1], base[kMaxExperts], rows[kMaxExperts];
 };
-constexpr int SMEM_BYTES = DATA + (int)sizeof(Smem) + 1024;
+// epilogue staging: each epilogue warp owns 32 rows x 128 B (+16 B pad against bank conflicts)
+constexpr int STAGE_ROW_BYTES = 144;
+constexpr int STAGE_WARP_BYTES = 32 * STAGE_ROW_BYTES;
+constexpr int SMEM_OFF_STAGE = DATA + (((int)sizeof(Smem) + 127) / 128) * 128;
+constexpr int SMEM_BYTES = SMEM_OFF_STAGE + 4 * STAGE_WARP_BYTES + 1024;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -279,6 +283,28 @@ __device__ __forceinline__ void tmem_wait_ld() {
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+// Store this warp's 32 rows x 64 bf16 columns (128 B per row): lane l holds row
+// l's 32 packed words in v and that row's destination in dst (nullptr = skip).
+// The rows go through the warp's shared-memory slice so that every store
+// instruction writes four whole 128-byte row segments (coalesced for HBM and
+// for NVLink when the destination is a peer's buffer).
+__device__ __forceinline__ void warp_store_rows(uint8_t* stage, const uint32_t (&v)[32],
+                                                void* dst, int lane) {
+  uint4* srow = reinterpret_cast<uint4*>(stage + lane * STAGE_ROW_BYTES);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) srow[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  __syncwarp();
+  const unsigned long long mine = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3), seg = lane & 7;
+    const unsigned long long d = __shfl_sync(0xffffffffu, mine, r);
+    const uint4 val = *reinterpret_cast<const uint4*>(stage + r * STAGE_ROW_BYTES + seg * 16);
+    if (d) reinterpret_cast<uint4*>(d)[seg] = val;
+  }
+  __syncwarp();
 }
 
 struct TcArgs {
@@ -431,52 +457,50 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
           decode_tile(t, args.ntiles_n, 1, BM, S->n_local, S->prefix, S->base, S->rows);
       const bool valid = m < c.rows;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
+      uint8_t* stage = smem + SMEM_OFF_STAGE + q * STAGE_WARP_BYTES;
       if (MODE == 0) {
-        bf16* dst = args.act + (int64_t)(c.row0 + m) * args.act_ld + c.nb * 128;
+        bf16* row = valid ? args.act + (int64_t)(c.row0 + m) * args.act_ld + c.nb * 128 : nullptr;
 #pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t g[32], u[32];
-          tmem_ld32(tbase + ch * 32, g);
-          tmem_ld32(tbase + 128 + ch * 32, u);
-          tmem_wait_ld();
-          uint32_t packed[16];
+        for (int c64 = 0; c64 < 2; ++c64) {
+          uint32_t packed[32];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float a0 = silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i]), true);
-            const float a1 =
-                silu_mul(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1]), true);
-            packed[i] = pack_bf16x2(a0, a1);
-          }
-          if (valid) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + ch * 32);
+          for (int half = 0; half < 2; ++half) {
+            uint32_t g[32], u[32];
+            const int col = c64 * 64 + half * 32;
+            tmem_ld32(tbase + col, g);
+            tmem_ld32(tbase + 128 + col, u);
+            tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
-                                 packed[4 * i + 3]);
+            for (int i = 0; i < 16; ++i) {
+              const float a0 =
+                  silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i]), true);
+              const float a1 =
+                  silu_mul(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1]), true);
+              packed[half * 16 + i] = pack_bf16x2(a0, a1);
+            }
           }
+          warp_store_rows(stage, packed, row ? row + c64 * 64 : nullptr, lane);
         }
       } else {
-        bf16* dst = nullptr;
+        bf16* row = nullptr;
         if (valid) {
           const int32_t mt = args.meta[c.row0 + m];
-          dst = static_cast<bf16*>(args.peers.yk[mt >> 24]) + (int64_t)(mt & 0xffffff) * args.H +
+          row = static_cast<bf16*>(args.peers.yk[mt >> 24]) + (int64_t)(mt & 0xffffff) * args.H +
                 c.nb * BN;
         }
 #pragma unroll 1
-        for (int ch = 0; ch < BN / 32; ++ch) {
-          uint32_t y[32];
-          tmem_ld32(tbase + ch * 32, y);
+        for (int c64 = 0; c64 < BN / 64; ++c64) {
+          uint32_t y0[32], y1[32], packed[32];
+          tmem_ld32(tbase + c64 * 64, y0);
+          tmem_ld32(tbase + c64 * 64 + 32, y1);
           tmem_wait_ld();
-          if (valid) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + ch * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              d4[i] = make_uint4(
-                  pack_bf16x2(__uint_as_float(y[8 * i]), __uint_as_float(y[8 * i + 1])),
-                  pack_bf16x2(__uint_as_float(y[8 * i + 2]), __uint_as_float(y[8 * i + 3])),
-                  pack_bf16x2(__uint_as_float(y[8 * i + 4]), __uint_as_float(y[8 * i + 5])),
-                  pack_bf16x2(__uint_as_float(y[8 * i + 6]), __uint_as_float(y[8 * i + 7])));
+          for (int i = 0; i < 16; ++i) {
+            packed[i] = pack_bf16x2(__uint_as_float(y0[2 * i]), __uint_as_float(y0[2 * i + 1]));
+            packed[16 + i] =
+                pack_bf16x2(__uint_as_float(y1[2 * i]), __uint_as_float(y1[2 * i + 1]));
           }
+          warp_store_rows(stage, packed, row ? row + c64 * 64 : nullptr, lane);
         }
       }
       fence_before();
