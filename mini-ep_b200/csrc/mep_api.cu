@@ -39,6 +39,7 @@ struct mep_ctx {
   uint32_t seq = 0;
   unsigned long long timeout_ns = 10ull * 1000 * 1000 * 1000;
   int force_simt = 0;
+  int tc_single_cta = 0;
   std::vector<int> placed, n_local_l;
   int cur_layer = -1, stage = 0;
   int64_t cur_n = 0;
@@ -414,6 +415,7 @@ int mep_expert_ffn(mep_ctx* c, const void* w_in, const void* w_out, int n_local,
   a.seq = c->seq;
   a.num_sms = c->num_sms;
   a.force_simt = c->force_simt;
+  a.tc_single_cta = c->tc_single_cta;
   a.n_local_weights = n_local;
   a.err = c->err_dev;
   // a rank without resident experts still runs the (empty) kernel to signal
@@ -530,6 +532,10 @@ int mep_set_option(mep_ctx* c, const char* name, int64_t value) {
   if (!c || !name) return MEP_ERR_INVALID;
   if (!std::strcmp(name, "force_simt")) {
     c->force_simt = value != 0;
+    return MEP_OK;
+  }
+  if (!std::strcmp(name, "tc_single_cta")) {
+    c->tc_single_cta = value != 0;
     return MEP_OK;
   }
   if (!std::strcmp(name, "timeout_ms")) {

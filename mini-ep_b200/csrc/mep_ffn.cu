@@ -48,17 +48,18 @@ struct TileCoord {
   int j, row0, rows, nb;
 };
 __device__ __forceinline__ TileCoord decode_tile(int t, int ntiles_n, int sub, int sub_rows,
-                                                 int n_local, const int* tile_prefix,
-                                                 const int* seg_base, const int* seg_rows) {
+                                                 int tile_rows, int n_local,
+                                                 const int* tile_prefix, const int* seg_base,
+                                                 const int* seg_rows) {
   TileCoord c;
   const int mt = t / ntiles_n;
   c.nb = t - mt * ntiles_n;
-  const int m128 = mt / sub;
-  const int part = mt - m128 * sub;
+  const int mtile = mt / sub;
+  const int part = mt - mtile * sub;
   int j = 0;
-  while (j + 1 < n_local && tile_prefix[j + 1] <= m128) ++j;
+  while (j + 1 < n_local && tile_prefix[j + 1] <= mtile) ++j;
   c.j = j;
-  const int local_row = (m128 - tile_prefix[j]) * kRowAlign + part * sub_rows;
+  const int local_row = (mtile - tile_prefix[j]) * tile_rows + part * sub_rows;
   c.row0 = seg_base[j] + local_row;
   c.rows = seg_rows[j] - local_row;
   return c;
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(256) k_ffn_simt(const T* __restrict__ A, int l
   const int total = lay->total_mtiles * 2 * ntiles_n;
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   for (int t = blockIdx.x; t < total; t += gridDim.x) {
-    const TileCoord c = decode_tile(t, ntiles_n, 2, kSimtBM, n_local, s_prefix, s_base, s_rows);
+    const TileCoord c = decode_tile(t, ntiles_n, 2, kSimtBM, kRowAlign, n_local, s_prefix, s_base, s_rows);
     if (c.rows <= 0) continue;  // second half of a partly filled 128-row tile
     // B rows of this tile: MODE 0 -> 32 gate rows then 32 up rows; MODE 1 -> 64 rows
     const int64_t bexp = (int64_t)c.j * b_rows_per_expert;
@@ -383,7 +384,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
       uint32_t ph = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const TileCoord c =
-            decode_tile(t, args.ntiles_n, 1, BM, S->n_local, S->prefix, S->base, S->rows);
+            decode_tile(t, args.ntiles_n, 1, BM, kRowAlign, S->n_local, S->prefix, S->base, S->rows);
         const int brow0 = c.j * args.b_rows_per_expert + c.nb * args.b_step;
         const int brow1 = brow0 + args.b_second;
         bool ok = true;
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
       if (!ok) break;
       fence_after();
       const TileCoord c =
-          decode_tile(t, args.ntiles_n, 1, BM, S->n_local, S->prefix, S->base, S->rows);
+          decode_tile(t, args.ntiles_n, 1, BM, kRowAlign, S->n_local, S->prefix, S->base, S->rows);
       const bool valid = m < c.rows;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
       uint8_t* stage = smem + SMEM_OFF_STAGE + q * STAGE_WARP_BYTES;
@@ -519,6 +520,302 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
   if (MODE == 1) grid_done_signal_ffn(args.done_ctr, args.peers, args.world, args.rank, args.seq);
 }
 
+// ---------------------------------------------------------------- CTA pairs
+// The same FFN with a pair of CTAs (a 2-CTA cluster) per 256x256 tile: the
+// leader CTA issues tcgen05.mma.cta_group::2 (M=256, N=256, K=16); each CTA
+// holds its own 128 rows of A and 128 of the 256 B rows in its shared memory
+// and its own 128 x 256 fp32 accumulator rows in its TMEM. Per k-block a CTA
+// loads 32 KB instead of 48 KB for the same tensor work, and six stages fit.
+// GEMM1's B split is natural: the leader loads the 128 gate rows, the other
+// CTA the 128 up rows. Both CTAs' TMA loads complete on the leader's "full"
+// barrier; the leader's MMA completion is committed to both CTAs' "empty" and
+// "accumulator full" barriers; both CTAs' epilogue warps arrive on the
+// leader's "accumulator empty" barrier. Expert segments are padded to 128
+// rows, so the second CTA of a pair tile may hold rows past the segment end:
+// those rows are computed and not stored.
+constexpr int P_STAGES = 6;
+constexpr int P_STAGE = A_STAGE + A_STAGE;           // 16 KB of A + 16 KB of B per CTA
+constexpr int P_DATA = P_STAGES * P_STAGE;
+constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(256 >> 4) << 24);
+
+struct PSmem {
+  uint64_t full[P_STAGES], empty[P_STAGES], tfull[2], tempty[2];
+  uint32_t tmem_base;
+  int abort;
+  int n_local, total;
+  int prefix[kMaxExperts + 1], base[kMaxExperts], rows[kMaxExperts];
+};
+constexpr int P_OFF_STAGE = P_DATA + (((int)sizeof(PSmem) + 127) / 128) * 128;
+constexpr int P_SMEM_BYTES = P_OFF_STAGE + 4 * STAGE_WARP_BYTES + 1024;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same location in CTA `cta` of this cluster
+__device__ __forceinline__ uint32_t map_to_cta(const void* p, uint32_t cta) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(cta));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA load into this CTA's shared memory whose bytes complete on the pair
+// leader's barrier (given as a shared::cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm, int x, int y,
+                                                 uint32_t leader_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(leader_bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a, uint64_t b,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// completion of this thread's prior pair MMAs arrives on the barrier at the
+// same offset in both CTAs of the pair
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  const uint16_t both = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(both)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_wait_p(uint64_t* b, uint32_t parity, PSmem* S, int* err) {
+  if (mbar_try(b, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try(b, parity)) return true;
+    if ((it & 63u) == 63u) {
+      if (*(volatile int*)&S->abort) return false;
+      if (globaltimer_ns() - t0 > kWaitNs) {
+        *(volatile int*)&S->abort = 1;
+        set_err(err, kErrPipeline);
+        return false;
+      }
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(THREADS, 1) k_ffn_tc_pair(const __grid_constant__ CUtensorMap tmA,
+                                                            const __grid_constant__ CUtensorMap tmB,
+                                                            const TcArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  PSmem* S = reinterpret_cast<PSmem*>(smem + P_DATA);
+  const int wp = warp_id(), lane = lane_id();
+  const uint32_t cta = cluster_rank();
+  const bool leader = cta == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&S->full[s], 1);
+      mbar_init(&S->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&S->tfull[b], 1);
+      mbar_init(&S->tempty[b], 8);  // 4 epilogue warps x 2 CTAs (used in the leader)
+    }
+    S->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (wp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&S->tmem_base)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  {
+    const Layout* lay = args.lay;
+    const int nl = lay->n_local;
+    if (threadIdx.x == 0) {
+      // 256-row pair tiles per local expert
+      int tiles = 0;
+      for (int j = 0; j < nl; ++j) {
+        S->prefix[j] = tiles;
+        tiles += (lay->seg_rows[j] + 255) / 256;
+      }
+      S->prefix[nl] = tiles;
+      S->n_local = nl;
+      S->total = lay->total_mtiles > 0 ? tiles * args.ntiles_n : 0;
+    }
+    for (int i = threadIdx.x; i < nl; i += blockDim.x) {
+      S->base[i] = lay->seg_base[i];
+      S->rows[i] = lay->seg_rows[i];
+    }
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers exist before any remote arrive or TMA completion
+  fence_after();
+  const uint32_t tmem_base = S->tmem_base;
+  const int total = S->total;
+  const int kblocks = args.K / BK;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (wp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int t = pair; t < total; t += npairs) {
+        const TileCoord c =
+            decode_tile(t, args.ntiles_n, 1, 256, 256, S->n_local, S->prefix, S->base, S->rows);
+        const int arow = c.row0 + (int)cta * 128;
+        const int brow = c.j * args.b_rows_per_expert + c.nb * args.b_step +
+                         (cta ? args.b_second : 0);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_p(&S->empty[s], ph ^ 1u, S, args.err)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_expect_tx(&S->full[s], 2 * P_STAGE);
+          const uint32_t lbar = map_to_cta(&S->full[s], 0);
+          uint8_t* st = smem + s * P_STAGE;
+          tma_load_2d_pair(st, &tmA, kb * BK, arow, lbar);
+          tma_load_2d_pair(st + A_STAGE, &tmB, kb * BK, brow, lbar);
+          if (++s == P_STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (wp == 1) {
+    if (leader && lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      for (int t = pair; t < total; t += npairs, ++it) {
+        const int b = it & 1;
+        const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+        if (!mbar_wait_p(&S->tempty[b], aph ^ 1u, S, args.err)) break;
+        fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_p(&S->full[s], ph, S, args.err)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t a0 = smem_u32(smem + s * P_STAGE);
+          const uint32_t b0 = a0 + A_STAGE;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_f16_pair(d_tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), P_IDESC,
+                         (kb | kk) != 0);
+          mma_commit_pair(&S->empty[s]);
+          if (++s == P_STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(&S->tfull[b]);
+      }
+    }
+  } else {
+    const int q = wp & 3;
+    const int m = q * 32 + lane;
+    const uint32_t leader_tempty[2] = {map_to_cta(&S->tempty[0], 0), map_to_cta(&S->tempty[1], 0)};
+    uint8_t* stage = smem + P_OFF_STAGE + q * STAGE_WARP_BYTES;
+    int it = 0;
+    for (int t = pair; t < total; t += npairs, ++it) {
+      const int b = it & 1;
+      const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_p(&S->tfull[b], aph, S, args.err);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      fence_after();
+      const TileCoord c =
+          decode_tile(t, args.ntiles_n, 1, 256, 256, S->n_local, S->prefix, S->base, S->rows);
+      const int r = (int)cta * 128 + m;  // row inside the 256-row pair tile
+      const bool valid = r < c.rows;
+      const int64_t grow = c.row0 + r;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
+      if (MODE == 0) {
+        bf16* row = valid ? args.act + grow * args.act_ld + c.nb * 128 : nullptr;
+#pragma unroll 1
+        for (int c64 = 0; c64 < 2; ++c64) {
+          uint32_t packed[32];
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t g[32], u[32];
+            const int col = c64 * 64 + half * 32;
+            tmem_ld32(tbase + col, g);
+            tmem_ld32(tbase + 128 + col, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float a0 =
+                  silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i]), true);
+              const float a1 =
+                  silu_mul(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1]), true);
+              packed[half * 16 + i] = pack_bf16x2(a0, a1);
+            }
+          }
+          warp_store_rows(stage, packed, row ? row + c64 * 64 : nullptr, lane);
+        }
+      } else {
+        bf16* row = nullptr;
+        if (valid) {
+          const int32_t mt = args.meta[grow];
+          row = static_cast<bf16*>(args.peers.yk[mt >> 24]) + (int64_t)(mt & 0xffffff) * args.H +
+                c.nb * BN;
+        }
+#pragma unroll 1
+        for (int c64 = 0; c64 < BN / 64; ++c64) {
+          uint32_t y0[32], y1[32], packed[32];
+          tmem_ld32(tbase + c64 * 64, y0);
+          tmem_ld32(tbase + c64 * 64 + 32, y1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            packed[i] = pack_bf16x2(__uint_as_float(y0[2 * i]), __uint_as_float(y0[2 * i + 1]));
+            packed[16 + i] =
+                pack_bf16x2(__uint_as_float(y1[2 * i]), __uint_as_float(y1[2 * i + 1]));
+          }
+          warp_store_rows(stage, packed, row ? row + c64 * 64 : nullptr, lane);
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(leader_tempty[b]);
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  cluster_sync();  // the pair's MMAs and remote arrivals are over before TMEM is freed
+  fence_after();
+  if (wp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  if (MODE == 1) grid_done_signal_ffn(args.done_ctr, args.peers, args.world, args.rank, args.seq);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
@@ -554,6 +851,12 @@ int tc_init() {
   if (cudaFuncSetAttribute(tc::k_ffn_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            tc::SMEM_BYTES) != cudaSuccess)
     return -2;
+  if (cudaFuncSetAttribute(tc::k_ffn_tc_pair<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::P_SMEM_BYTES) != cudaSuccess)
+    return -2;
+  if (cudaFuncSetAttribute(tc::k_ffn_tc_pair<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::P_SMEM_BYTES) != cudaSuccess)
+    return -2;
   tc::g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   return 0;
 }
@@ -580,7 +883,30 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g1.act = static_cast<bf16*>(a.act);
     g1.act_ld = I;
     g1.err = a.err;
-    tc::k_ffn_tc<0><<<a.num_sms, tc::THREADS, tc::SMEM_BYTES, st>>>(tmA1, tmB1, g1);
+    const bool pair = !a.tc_single_cta && a.num_sms >= 2;
+    const int pair_grid = a.num_sms & ~1;
+    auto launch_pair = [&](auto kernel, const CUtensorMap& ta, const CUtensorMap& tb,
+                           const tc::TcArgs& g) -> cudaError_t {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3((unsigned)pair_grid);
+      cfg.blockDim = dim3(tc::THREADS);
+      cfg.dynamicSmemBytes = tc::P_SMEM_BYTES;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      return cudaLaunchKernelEx(&cfg, kernel, ta, tb, g);
+    };
+    if (pair) {
+      const cudaError_t e = launch_pair(tc::k_ffn_tc_pair<0>, tmA1, tmB1, g1);
+      if (e != cudaSuccess) return (int)e;
+    } else {
+      tc::k_ffn_tc<0><<<a.num_sms, tc::THREADS, tc::SMEM_BYTES, st>>>(tmA1, tmB1, g1);
+    }
     tc::TcArgs g2{};
     g2.lay = a.layout;
     g2.K = I;
@@ -596,7 +922,12 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g2.done_ctr = a.done_ctr;
     g2.seq = a.seq;
     g2.err = a.err;
-    tc::k_ffn_tc<1><<<a.num_sms, tc::THREADS, tc::SMEM_BYTES, st>>>(tmA2, tmB2, g2);
+    if (pair) {
+      const cudaError_t e = launch_pair(tc::k_ffn_tc_pair<1>, tmA2, tmB2, g2);
+      if (e != cudaSuccess) return (int)e;
+    } else {
+      tc::k_ffn_tc<1><<<a.num_sms, tc::THREADS, tc::SMEM_BYTES, st>>>(tmA2, tmB2, g2);
+    }
     return (int)cudaGetLastError();
   }
   if (H % kSimtBN != 0 || I % 32 != 0) return -3;

@@ -111,6 +111,7 @@ struct FfnArgs {
   uint32_t seq;
   int num_sms;
   int force_simt;           // 1: run the CUDA-core kernels even for bf16
+  int tc_single_cta;        // 1: one CTA per 128x256 tile instead of CTA pairs per 256x256
   int n_local_weights;      // leading extent of w_in / w_out
   int* err;                 // host-mapped device error word
 };

@@ -23,13 +23,16 @@ def world1_comm(E, topk, H, I, max_tokens, dtype):
     return comm
 
 
-def world1_backend(w_in, w_out, topk, max_tokens, stats=True, num_layers=1, force_simt=False):
+def world1_backend(w_in, w_out, topk, max_tokens, stats=True, num_layers=1, force_simt=False,
+                   single_cta=False):
     """A one-rank expert-parallel backend holding all experts of layer 0."""
     E, two_i, H = w_in.shape
     comm = Comm(num_layers=num_layers, num_experts=E, topk=topk, hidden=H, inter=two_i // 2,
                 max_tokens=max_tokens, dtype=w_in.dtype, single_process=True, timeout_ms=5000)
     if force_simt:
         comm.set_option("force_simt", 1)
+    if single_cta:
+        comm.set_option("tc_single_cta", 1)
     placement = Placement.naive(num_layers, E, 1)
     comm.install(placement)
     st = EPStats(num_layers, E) if stats else None

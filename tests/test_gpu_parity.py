@@ -148,14 +148,16 @@ def test_layer_fp32_config1_matches_reference(golden):
     be.comm.check()
 
 
-@pytest.mark.parametrize("force_simt", [False, True], ids=["tcgen05", "cuda_cores"])
+@pytest.mark.parametrize("path", ["tcgen05_pair", "tcgen05_single", "cuda_cores"])
 @pytest.mark.parametrize("n", [1, 127, 300, 2048])
-def test_layer_bf16_shape_a(n, force_simt):
+def test_layer_bf16_shape_a(n, path):
+    force_simt, single_cta = path == "cuda_cores", path == "tcgen05_single"
     sh = synth.SHAPES["a"]
     lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=2, dtype=torch.bfloat16)
     bias = synth.zipf_router_bias(1, sh["experts"])[0]
     idx, gate, _ = O.router_topk(lb.x, lb.router, sh["topk"], bias)
-    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], max(n, 256), force_simt=force_simt)
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], max(n, 256), force_simt=force_simt,
+                        single_cta=single_cta)
     out = be(lb.x.cuda(), idx.cuda(), gate.cuda()).cpu()
     ref32 = _fp32_ref(lb.x, idx, gate, lb.w_in, lb.w_out)
     assert (out.float() - ref32).abs().max() <= BF16_ATOL
@@ -173,12 +175,15 @@ def test_tcgen05_and_cuda_core_paths_agree():
     idx, gate, _ = O.router_topk(lb.x, lb.router, sh["topk"], synth.zipf_router_bias(1, 32)[0])
     a = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
     b = world1_backend(lb.w_in, lb.w_out, sh["topk"], n, force_simt=True)
+    c = world1_backend(lb.w_in, lb.w_out, sh["topk"], n, single_cta=True)
     xa, ia, ga = lb.x.cuda(), idx.cuda(), gate.cuda()
-    oa, ob = a(xa, ia, ga), b(xa, ia, ga)
+    oa, ob, oc = a(xa, ia, ga), b(xa, ia, ga), c(xa, ia, ga)
     d = (oa.float() - ob.float()).abs()
     assert d.max() <= 1e-2 and (d == 0).float().mean() > 0.9
-    a.comm.check()
-    b.comm.check()
+    # CTA pairs and single CTAs run the same MMA chain per row: identical bits
+    assert torch.equal(oa, oc)
+    for be in (a, b, c):
+        be.comm.check()
 
 
 def test_layer_bf16_shape_b():
