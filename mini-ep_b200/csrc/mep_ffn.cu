@@ -6,13 +6,15 @@
 //                                      source rank's (token, slot) landing row.
 //
 // Two implementations share the tile schedule (Layout: expert segments padded
-// to 128 rows, tile t -> (segment, 128-row block, N block)):
+// to 128 rows, tile t -> (segment, row tile, N block)):
 //   * tcgen05 (bf16): persistent, warp-specialised kernel. Warp 0 issues TMA
-//     loads (128B-swizzled K-major tiles) into a 4-stage shared-memory ring,
-//     warp 1 issues tcgen05.mma (M=128, N=256, K=16) into a double-buffered
-//     TMEM accumulator (2 x 256 columns), warps 2-5 drain TMEM with
-//     tcgen05.ld and run the epilogue (SwiGLU, or the store to the source
-//     rank's landing buffer over NVLink) while the next tile accumulates.
+//     loads (128B-swizzled K-major tiles) into a shared-memory stage ring,
+//     warp 1 issues tcgen05.mma (N=256, K=16) into a double-buffered TMEM
+//     accumulator (2 x 256 columns), warps 2-9 drain TMEM with tcgen05.ld and
+//     run the epilogue (SwiGLU, or the store to the source rank's landing
+//     buffer over NVLink) while the next tile accumulates. By default a pair
+//     of CTAs (2-CTA cluster, tcgen05.mma.cta_group::2) computes a 256x256
+//     tile; the single-CTA 128x256 variant stays selectable.
 //     GEMM1 puts the gate rows [n, n+128) and the up rows [I+n, I+n+128) of
 //     w_in side by side in one 256-row B tile, so one MMA chain produces both
 //     halves of the SwiGLU for the same rows.
@@ -164,29 +166,50 @@ __global__ void __launch_bounds__(256) k_ffn_simt(const T* __restrict__ A, int l
 
 // =================================================================== tcgen05
 namespace tc {
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_STAGE = BM * BK * 2;            // 16 KiB
-constexpr int B_STAGE = BN * BK * 2;            // 32 KiB
-constexpr int DATA = STAGES * (A_STAGE + B_STAGE);
-constexpr int THREADS = 192;                    // warp0 TMA, warp1 MMA, warps 2-5 epilogue
+constexpr int BN = 256, BK = 64;
+constexpr int A_TILE = 128 * BK * 2;            // 16 KiB: 128 rows x 64 bf16 (one 128B-swizzle row each)
+constexpr int EPI_WARPS = 8;                    // two per TMEM lane quadrant, splitting the columns
+constexpr int THREADS = 64 + 32 * EPI_WARPS;    // warp0 TMA, warp1 MMA, warps 2-9 epilogue
 constexpr int TMEM_COLS = 512;                  // two 256-column fp32 accumulators
 constexpr unsigned long long kWaitNs = 2000000000ull;  // bounded mbarrier waits (2 s)
-// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, N=256, M=128
-constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
 
+// Per-variant geometry. Single CTA: a 128x256 tile per CTA, the CTA loads
+// 128 A rows + 256 B rows per k-block. CTA pair: a 256x256 tile per 2-CTA
+// cluster, each CTA loads its 128 A rows + 128 of the B rows.
+template <bool PAIR>
+struct Geo {
+  static constexpr int TILE_M = PAIR ? 256 : 128;
+  static constexpr int B_ROWS = PAIR ? 128 : 256;         // B rows held by one CTA
+  static constexpr int STAGE = A_TILE + B_ROWS * BK * 2;  // bytes per stage per CTA
+  static constexpr int STAGES = PAIR ? 6 : 4;
+  static constexpr int DATA = STAGES * STAGE;
+  static constexpr uint32_t TX = (PAIR ? 2 : 1) * STAGE;  // bytes landing on the leader's barrier
+  // kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, N=256, M=TILE_M
+  static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
+                                    ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TILE_M >> 4) << 24);
+  static constexpr uint32_t TEMPTY_ARRIVALS = EPI_WARPS * (PAIR ? 2 : 1);
+};
+
+template <bool PAIR>
 struct Smem {
-  uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
+  uint64_t full[Geo<PAIR>::STAGES], empty[Geo<PAIR>::STAGES], tfull[2], tempty[2];
   uint32_t tmem_base;
   int abort;
   int n_local, total;
   int prefix[kMaxExperts + 1], base[kMaxExperts], rows[kMaxExperts];
 };
-// epilogue staging: each epilogue warp owns 32 rows x 128 B (+16 B pad against bank conflicts)
-constexpr int STAGE_ROW_BYTES = 144;
-constexpr int STAGE_WARP_BYTES = 32 * STAGE_ROW_BYTES;
-constexpr int SMEM_OFF_STAGE = DATA + (((int)sizeof(Smem) + 127) / 128) * 128;
-constexpr int SMEM_BYTES = SMEM_OFF_STAGE + 4 * STAGE_WARP_BYTES + 1024;
+// epilogue staging: 32 rows x 128 B per warp, 16-byte chunks XOR-swizzled by row
+constexpr int STAGE_WARP_BYTES = 32 * 128;
+template <bool PAIR>
+constexpr int off_stage() {
+  return Geo<PAIR>::DATA + (((int)sizeof(Smem<PAIR>) + 127) / 128) * 128;
+}
+template <bool PAIR>
+constexpr int smem_bytes() {
+  return off_stage<PAIR>() + EPI_WARPS * STAGE_WARP_BYTES + 1024;
+}
+static_assert(smem_bytes<false>() <= 232448, "single-CTA kernel exceeds shared memory");
+static_assert(smem_bytes<true>() <= 232448, "CTA-pair kernel exceeds shared memory");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -198,9 +221,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
                "r"(bytes)
                : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
 __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
   uint32_t ok;
@@ -215,7 +235,8 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
 }
 // Bounded wait: false (and the CTA abort flag + device error set) on timeout
 // or when another role of this CTA already gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, Smem* S, int* err) {
+template <bool PAIR>
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, Smem<PAIR>* S, int* err) {
   if (mbar_try(b, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 0;; ++it) {
@@ -230,13 +251,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, Smem* S,
     }
   }
 }
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same location in CTA `cta` of this cluster
+__device__ __forceinline__ uint32_t map_to_cta(const void* p, uint32_t cta) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(cta));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 2D TMA tile load into this CTA's shared memory. Single CTA: completes on
+// this CTA's barrier. Pair: completes on the pair leader's barrier, given as
+// a shared::cluster address.
+template <bool PAIR>
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
+                                            uint32_t bar) {
+  if (PAIR)
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+  else
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
 }
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
@@ -246,19 +293,43 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   d |= (uint64_t)2 << 61;             // 128-byte swizzle
   return d;
 }
+template <bool PAIR>
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  if (PAIR)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
+// completion of this thread's prior MMAs arrives on `bar` (pair: on the
+// barrier at the same offset in both CTAs)
+template <bool PAIR>
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
+  if (PAIR) {
+    const uint16_t both = 0x3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(smem_u32(bar)),
+        "h"(both)
+        : "memory");
+  } else {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+  }
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
 }
 __device__ __forceinline__ void fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -285,24 +356,39 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&p);
 }
+__device__ __forceinline__ float bf16_round(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+// silu(bf16(g)) rounded to bf16, times bf16(u): the rounding points of the
+// reference's bf16 SwiGLU (modeling.py:102-103). The fp32 sigmoid uses the
+// fast exponential and division intrinsics (a few fp32 ulp from the exact
+// expressions, far inside one bf16 rounding step).
+__device__ __forceinline__ float swiglu_bf16(float g, float u) {
+  const float gr = bf16_round(g);
+  const float s = bf16_round(__fdividef(gr, 1.f + __expf(-gr)));
+  return s * bf16_round(u);
+}
 
 // Store this warp's 32 rows x 64 bf16 columns (128 B per row): lane l holds row
 // l's 32 packed words in v and that row's destination in dst (nullptr = skip).
-// The rows go through the warp's shared-memory slice so that every store
+// The rows go through the warp's shared-memory slice (16-byte chunks
+// XOR-swizzled by row, conflict-free both ways) so that every store
 // instruction writes four whole 128-byte row segments (coalesced for HBM and
 // for NVLink when the destination is a peer's buffer).
 __device__ __forceinline__ void warp_store_rows(uint8_t* stage, const uint32_t (&v)[32],
                                                 void* dst, int lane) {
-  uint4* srow = reinterpret_cast<uint4*>(stage + lane * STAGE_ROW_BYTES);
+  uint8_t* srow = stage + lane * 128;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) srow[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  for (int i = 0; i < 8; ++i)
+    *reinterpret_cast<uint4*>(srow + ((i ^ (lane & 7)) << 4)) =
+        make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   __syncwarp();
   const unsigned long long mine = reinterpret_cast<unsigned long long>(dst);
 #pragma unroll
   for (int it = 0; it < 8; ++it) {
     const int r = it * 4 + (lane >> 3), seg = lane & 7;
     const unsigned long long d = __shfl_sync(0xffffffffu, mine, r);
-    const uint4 val = *reinterpret_cast<const uint4*>(stage + r * STAGE_ROW_BYTES + seg * 16);
+    const uint4 val = *reinterpret_cast<const uint4*>(stage + r * 128 + ((seg ^ (r & 7)) << 4));
     if (d) reinterpret_cast<uint4*>(d)[seg] = val;
   }
   __syncwarp();
@@ -311,7 +397,7 @@ __device__ __forceinline__ void warp_store_rows(uint8_t* stage, const uint32_t (
 struct TcArgs {
   const Layout* lay;
   int K;                   // reduction length
-  int ntiles_n;            // N blocks per 128-row tile
+  int ntiles_n;            // N blocks per row tile
   int b_rows_per_expert;   // rows of B per local expert (2I or H)
   int b_step;              // B rows advanced per N block (128 for GEMM1, 256 for GEMM2)
   int b_second;            // offset of the second 128-row half of the B tile
@@ -326,332 +412,55 @@ struct TcArgs {
 };
 
 // MODE 0: GEMM1 + SwiGLU -> act. MODE 1: GEMM2 -> source landing rows.
-template <int MODE>
+// PAIR: one 256-row tile per 2-CTA cluster with tcgen05.mma.cta_group::2.
+template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ CUtensorMap tmA,
                                                        const __grid_constant__ CUtensorMap tmB,
                                                        const TcArgs args) {
+  using G = Geo<PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_STAGE;
-  Smem* S = reinterpret_cast<Smem*>(smem + DATA);
+  Smem<PAIR>* S = reinterpret_cast<Smem<PAIR>*>(smem + G::DATA);
   const int wp = warp_id(), lane = lane_id();
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&S->full[s], 1);
-      mbar_init(&S->empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&S->tfull[b], 1);
-      mbar_init(&S->tempty[b], 4);
-    }
-    S->abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
-  if (wp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(&S->tmem_base)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  {
-    const Layout* lay = args.lay;
-    const int nl = lay->n_local;
-    if (threadIdx.x == 0) {
-      S->n_local = nl;
-      S->total = lay->total_mtiles * args.ntiles_n;
-    }
-    for (int i = threadIdx.x; i <= nl; i += blockDim.x) S->prefix[i] = lay->tile_prefix[i];
-    for (int i = threadIdx.x; i < nl; i += blockDim.x) {
-      S->base[i] = lay->seg_base[i];
-      S->rows[i] = lay->seg_rows[i];
-    }
-  }
-  fence_before();
-  __syncthreads();
-  fence_after();
-  const uint32_t tmem_base = S->tmem_base;
-  const int total = S->total;
-  const int kblocks = args.K / BK;
-
-  if (wp == 0) {
-    if (lane == 0) {
-      int s = 0;
-      uint32_t ph = 0;
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        const TileCoord c =
-            decode_tile(t, args.ntiles_n, 1, BM, kRowAlign, S->n_local, S->prefix, S->base, S->rows);
-        const int brow0 = c.j * args.b_rows_per_expert + c.nb * args.b_step;
-        const int brow1 = brow0 + args.b_second;
-        bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&S->empty[s], ph ^ 1u, S, args.err)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(&S->full[s], A_STAGE + B_STAGE);
-          tma_load_2d(sA + s * A_STAGE, &tmA, kb * BK, c.row0, &S->full[s]);
-          tma_load_2d(sB + s * B_STAGE, &tmB, kb * BK, brow0, &S->full[s]);
-          tma_load_2d(sB + s * B_STAGE + B_STAGE / 2, &tmB, kb * BK, brow1, &S->full[s]);
-          if (++s == STAGES) {
-            s = 0;
-            ph ^= 1u;
-          }
-        }
-        if (!ok) break;
-      }
-    }
-  } else if (wp == 1) {
-    if (lane == 0) {
-      int s = 0;
-      uint32_t ph = 0;
-      int it = 0;
-      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-        const int b = it & 1;
-        const uint32_t aph = (uint32_t)(it >> 1) & 1u;
-        if (!mbar_wait(&S->tempty[b], aph ^ 1u, S, args.err)) break;
-        fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
-        bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&S->full[s], ph, S, args.err)) {
-            ok = false;
-            break;
-          }
-          fence_after();
-          const uint32_t a0 = smem_u32(sA + s * A_STAGE);
-          const uint32_t b0 = smem_u32(sB + s * B_STAGE);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            mma_f16(d_tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), IDESC,
-                    (kb | kk) != 0);
-          mma_commit(&S->empty[s]);
-          if (++s == STAGES) {
-            s = 0;
-            ph ^= 1u;
-          }
-        }
-        if (!ok) break;
-        mma_commit(&S->tfull[b]);
-      }
-    }
-  } else {
-    // epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32)
-    const int q = wp & 3;
-    const int m = q * 32 + lane;
-    int it = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-      const int b = it & 1;
-      const uint32_t aph = (uint32_t)(it >> 1) & 1u;
-      // one lane waits, the warp follows its verdict: the TMEM loads below are
-      // warp-collective, so the warp must never split on a timeout
-      int ok = 1;
-      if (lane == 0) ok = mbar_wait(&S->tfull[b], aph, S, args.err);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      fence_after();
-      const TileCoord c =
-          decode_tile(t, args.ntiles_n, 1, BM, kRowAlign, S->n_local, S->prefix, S->base, S->rows);
-      const bool valid = m < c.rows;
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
-      uint8_t* stage = smem + SMEM_OFF_STAGE + q * STAGE_WARP_BYTES;
-      if (MODE == 0) {
-        bf16* row = valid ? args.act + (int64_t)(c.row0 + m) * args.act_ld + c.nb * 128 : nullptr;
-#pragma unroll 1
-        for (int c64 = 0; c64 < 2; ++c64) {
-          uint32_t packed[32];
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t g[32], u[32];
-            const int col = c64 * 64 + half * 32;
-            tmem_ld32(tbase + col, g);
-            tmem_ld32(tbase + 128 + col, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float a0 =
-                  silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i]), true);
-              const float a1 =
-                  silu_mul(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1]), true);
-              packed[half * 16 + i] = pack_bf16x2(a0, a1);
-            }
-          }
-          warp_store_rows(stage, packed, row ? row + c64 * 64 : nullptr, lane);
-        }
-      } else {
-        bf16* row = nullptr;
-        if (valid) {
-          const int32_t mt = args.meta[c.row0 + m];
-          row = static_cast<bf16*>(args.peers.yk[mt >> 24]) + (int64_t)(mt & 0xffffff) * args.H +
-                c.nb * BN;
-        }
-#pragma unroll 1
-        for (int c64 = 0; c64 < BN / 64; ++c64) {
-          uint32_t y0[32], y1[32], packed[32];
-          tmem_ld32(tbase + c64 * 64, y0);
-          tmem_ld32(tbase + c64 * 64 + 32, y1);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            packed[i] = pack_bf16x2(__uint_as_float(y0[2 * i]), __uint_as_float(y0[2 * i + 1]));
-            packed[16 + i] =
-                pack_bf16x2(__uint_as_float(y1[2 * i]), __uint_as_float(y1[2 * i + 1]));
-          }
-          warp_store_rows(stage, packed, row ? row + c64 * 64 : nullptr, lane);
-        }
-      }
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S->tempty[b]);
-    }
-  }
-
-  fence_before();
-  __syncthreads();
-  fence_after();
-  if (wp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(TMEM_COLS)
-                 : "memory");
-  if (MODE == 1) grid_done_signal_ffn(args.done_ctr, args.peers, args.world, args.rank, args.seq);
-}
-
-// ---------------------------------------------------------------- CTA pairs
-// The same FFN with a pair of CTAs (a 2-CTA cluster) per 256x256 tile: the
-// leader CTA issues tcgen05.mma.cta_group::2 (M=256, N=256, K=16); each CTA
-// holds its own 128 rows of A and 128 of the 256 B rows in its shared memory
-// and its own 128 x 256 fp32 accumulator rows in its TMEM. Per k-block a CTA
-// loads 32 KB instead of 48 KB for the same tensor work, and six stages fit.
-// GEMM1's B split is natural: the leader loads the 128 gate rows, the other
-// CTA the 128 up rows. Both CTAs' TMA loads complete on the leader's "full"
-// barrier; the leader's MMA completion is committed to both CTAs' "empty" and
-// "accumulator full" barriers; both CTAs' epilogue warps arrive on the
-// leader's "accumulator empty" barrier. Expert segments are padded to 128
-// rows, so the second CTA of a pair tile may hold rows past the segment end:
-// those rows are computed and not stored.
-constexpr int P_STAGES = 6;
-constexpr int P_STAGE = A_STAGE + A_STAGE;           // 16 KB of A + 16 KB of B per CTA
-constexpr int P_DATA = P_STAGES * P_STAGE;
-constexpr uint32_t P_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                             ((uint32_t)(256 >> 4) << 24);
-
-struct PSmem {
-  uint64_t full[P_STAGES], empty[P_STAGES], tfull[2], tempty[2];
-  uint32_t tmem_base;
-  int abort;
-  int n_local, total;
-  int prefix[kMaxExperts + 1], base[kMaxExperts], rows[kMaxExperts];
-};
-constexpr int P_OFF_STAGE = P_DATA + (((int)sizeof(PSmem) + 127) / 128) * 128;
-constexpr int P_SMEM_BYTES = P_OFF_STAGE + 4 * STAGE_WARP_BYTES + 1024;
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// shared::cluster address of the same location in CTA `cta` of this cluster
-__device__ __forceinline__ uint32_t map_to_cta(const void* p, uint32_t cta) {
-  uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(cta));
-  return out;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// TMA load into this CTA's shared memory whose bytes complete on the pair
-// leader's barrier (given as a shared::cluster address)
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm, int x, int y,
-                                                 uint32_t leader_bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(leader_bar)
-      : "memory");
-}
-__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a, uint64_t b,
-                                             uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-}
-// completion of this thread's prior pair MMAs arrives on the barrier at the
-// same offset in both CTAs of the pair
-__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
-  const uint16_t both = 0x3;
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(smem_u32(bar)),
-      "h"(both)
-      : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_wait_p(uint64_t* b, uint32_t parity, PSmem* S, int* err) {
-  if (mbar_try(b, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try(b, parity)) return true;
-    if ((it & 63u) == 63u) {
-      if (*(volatile int*)&S->abort) return false;
-      if (globaltimer_ns() - t0 > kWaitNs) {
-        *(volatile int*)&S->abort = 1;
-        set_err(err, kErrPipeline);
-        return false;
-      }
-    }
-  }
-}
-
-template <int MODE>
-__global__ void __launch_bounds__(THREADS, 1) k_ffn_tc_pair(const __grid_constant__ CUtensorMap tmA,
-                                                            const __grid_constant__ CUtensorMap tmB,
-                                                            const TcArgs args) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  PSmem* S = reinterpret_cast<PSmem*>(smem + P_DATA);
-  const int wp = warp_id(), lane = lane_id();
-  const uint32_t cta = cluster_rank();
+  const uint32_t cta = PAIR ? cluster_rank() : 0u;
   const bool leader = cta == 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P_STAGES; ++s) {
+    for (int s = 0; s < G::STAGES; ++s) {
       mbar_init(&S->full[s], 1);
       mbar_init(&S->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&S->tfull[b], 1);
-      mbar_init(&S->tempty[b], 8);  // 4 epilogue warps x 2 CTAs (used in the leader)
+      mbar_init(&S->tempty[b], G::TEMPTY_ARRIVALS);  // used in the leader
     }
     S->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (wp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(&S->tmem_base)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&S->tmem_base)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&S->tmem_base)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   {
     const Layout* lay = args.lay;
     const int nl = lay->n_local;
     if (threadIdx.x == 0) {
-      // 256-row pair tiles per local expert
-      int tiles = 0;
+      int tiles = 0;  // row tiles of TILE_M rows per local expert
       for (int j = 0; j < nl; ++j) {
         S->prefix[j] = tiles;
-        tiles += (lay->seg_rows[j] + 255) / 256;
+        tiles += (lay->seg_rows[j] + G::TILE_M - 1) / G::TILE_M;
       }
       S->prefix[nl] = tiles;
       S->n_local = nl;
@@ -664,35 +473,41 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc_pair(const __grid_constan
   }
   fence_before();
   __syncthreads();
-  cluster_sync();  // the peer's barriers exist before any remote arrive or TMA completion
+  if (PAIR) cluster_sync();  // the peer's barriers exist before any remote arrive or TMA completion
   fence_after();
   const uint32_t tmem_base = S->tmem_base;
   const int total = S->total;
   const int kblocks = args.K / BK;
-  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int nunits = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (wp == 0) {
+    // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      for (int t = pair; t < total; t += npairs) {
-        const TileCoord c =
-            decode_tile(t, args.ntiles_n, 1, 256, 256, S->n_local, S->prefix, S->base, S->rows);
+      for (int t = unit; t < total; t += nunits) {
+        const TileCoord c = decode_tile(t, args.ntiles_n, 1, G::TILE_M, G::TILE_M, S->n_local,
+                                        S->prefix, S->base, S->rows);
         const int arow = c.row0 + (int)cta * 128;
-        const int brow = c.j * args.b_rows_per_expert + c.nb * args.b_step +
-                         (cta ? args.b_second : 0);
+        const int brow = c.j * args.b_rows_per_expert + c.nb * args.b_step;
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait_p(&S->empty[s], ph ^ 1u, S, args.err)) {
+          if (!mbar_wait(&S->empty[s], ph ^ 1u, S, args.err)) {
             ok = false;
             break;
           }
-          if (leader) mbar_expect_tx(&S->full[s], 2 * P_STAGE);
-          const uint32_t lbar = map_to_cta(&S->full[s], 0);
-          uint8_t* st = smem + s * P_STAGE;
-          tma_load_2d_pair(st, &tmA, kb * BK, arow, lbar);
-          tma_load_2d_pair(st + A_STAGE, &tmB, kb * BK, brow, lbar);
-          if (++s == P_STAGES) {
+          if (leader) mbar_expect_tx(&S->full[s], G::TX);
+          const uint32_t bar = PAIR ? map_to_cta(&S->full[s], 0) : smem_u32(&S->full[s]);
+          uint8_t* st = smem + s * G::STAGE;
+          tma_load_2d<PAIR>(st, &tmA, kb * BK, arow, bar);
+          if (PAIR) {
+            tma_load_2d<PAIR>(st + A_TILE, &tmB, kb * BK, brow + (cta ? args.b_second : 0), bar);
+          } else {
+            tma_load_2d<PAIR>(st + A_TILE, &tmB, kb * BK, brow, bar);
+            tma_load_2d<PAIR>(st + A_TILE + A_TILE, &tmB, kb * BK, brow + args.b_second, bar);
+          }
+          if (++s == G::STAGES) {
             s = 0;
             ph ^= 1u;
           }
@@ -701,94 +516,99 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc_pair(const __grid_constan
       }
     }
   } else if (wp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader)
     if (leader && lane == 0) {
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
-      for (int t = pair; t < total; t += npairs, ++it) {
+      for (int t = unit; t < total; t += nunits, ++it) {
         const int b = it & 1;
         const uint32_t aph = (uint32_t)(it >> 1) & 1u;
-        if (!mbar_wait_p(&S->tempty[b], aph ^ 1u, S, args.err)) break;
+        if (!mbar_wait(&S->tempty[b], aph ^ 1u, S, args.err)) break;
         fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait_p(&S->full[s], ph, S, args.err)) {
+          if (!mbar_wait(&S->full[s], ph, S, args.err)) {
             ok = false;
             break;
           }
           fence_after();
-          const uint32_t a0 = smem_u32(smem + s * P_STAGE);
-          const uint32_t b0 = a0 + A_STAGE;
+          const uint32_t a0 = smem_u32(smem + s * G::STAGE);
+          const uint32_t b0 = a0 + A_TILE;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            mma_f16_pair(d_tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), P_IDESC,
-                         (kb | kk) != 0);
-          mma_commit_pair(&S->empty[s]);
-          if (++s == P_STAGES) {
+            mma_f16<PAIR>(d_tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), G::IDESC,
+                          (kb | kk) != 0);
+          mma_commit<PAIR>(&S->empty[s]);
+          if (++s == G::STAGES) {
             s = 0;
             ph ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit_pair(&S->tfull[b]);
+        mma_commit<PAIR>(&S->tfull[b]);
       }
     }
   } else {
-    const int q = wp & 3;
+    // ---------------------------------------------------------------- epilogue
+    // warp wp may read TMEM lanes [32*(wp%4), +32) only; the two warps of a
+    // quadrant split the columns (h = 0, 1)
+    const int e = wp - 2;
+    const int q = wp & 3, h = e >> 2;
     const int m = q * 32 + lane;
-    const uint32_t leader_tempty[2] = {map_to_cta(&S->tempty[0], 0), map_to_cta(&S->tempty[1], 0)};
-    uint8_t* stage = smem + P_OFF_STAGE + q * STAGE_WARP_BYTES;
+    const uint32_t tempty_leader[2] = {PAIR ? map_to_cta(&S->tempty[0], 0) : smem_u32(&S->tempty[0]),
+                                       PAIR ? map_to_cta(&S->tempty[1], 0) : smem_u32(&S->tempty[1])};
+    uint8_t* stage = smem + off_stage<PAIR>() + e * STAGE_WARP_BYTES;
     int it = 0;
-    for (int t = pair; t < total; t += npairs, ++it) {
+    for (int t = unit; t < total; t += nunits, ++it) {
       const int b = it & 1;
       const uint32_t aph = (uint32_t)(it >> 1) & 1u;
+      const TileCoord c = decode_tile(t, args.ntiles_n, 1, G::TILE_M, G::TILE_M, S->n_local,
+                                      S->prefix, S->base, S->rows);
+      const int r = (int)cta * 128 + m;  // row inside the tile
+      const bool valid = r < c.rows;
+      const int64_t grow = c.row0 + r;
+      int32_t mt = 0;
+      if (MODE == 1 && valid) mt = args.meta[grow];  // in flight while the accumulator fills
+      // one lane waits, the warp follows its verdict: the TMEM loads below are
+      // warp-collective, so the warp must never split on a timeout
       int ok = 1;
-      if (lane == 0) ok = mbar_wait_p(&S->tfull[b], aph, S, args.err);
+      if (lane == 0) ok = mbar_wait(&S->tfull[b], aph, S, args.err);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       fence_after();
-      const TileCoord c =
-          decode_tile(t, args.ntiles_n, 1, 256, 256, S->n_local, S->prefix, S->base, S->rows);
-      const int r = (int)cta * 128 + m;  // row inside the 256-row pair tile
-      const bool valid = r < c.rows;
-      const int64_t grow = c.row0 + r;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
       if (MODE == 0) {
-        bf16* row = valid ? args.act + grow * args.act_ld + c.nb * 128 : nullptr;
+        // act columns [h*64, h*64+64) of this tile: gate at TMEM columns
+        // h*64.., up at 128 + h*64..
+        uint32_t packed[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t g[32], u[32];
+          const int col = h * 64 + half * 32;
+          tmem_ld32(tbase + col, g);
+          tmem_ld32(tbase + 128 + col, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            packed[half * 16 + i] =
+                pack_bf16x2(swiglu_bf16(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i])),
+                            swiglu_bf16(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1])));
+        }
+        bf16* row = valid ? args.act + grow * args.act_ld + c.nb * 128 + h * 64 : nullptr;
+        warp_store_rows(stage, packed, row, lane);
+      } else {
+        // output columns [h*128, h*128+128) of this tile, 64 at a time
+        bf16* row = valid ? static_cast<bf16*>(args.peers.yk[mt >> 24]) +
+                                (int64_t)(mt & 0xffffff) * args.H + c.nb * BN + h * 128
+                          : nullptr;
 #pragma unroll 1
         for (int c64 = 0; c64 < 2; ++c64) {
-          uint32_t packed[32];
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t g[32], u[32];
-            const int col = c64 * 64 + half * 32;
-            tmem_ld32(tbase + col, g);
-            tmem_ld32(tbase + 128 + col, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float a0 =
-                  silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i]), true);
-              const float a1 =
-                  silu_mul(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1]), true);
-              packed[half * 16 + i] = pack_bf16x2(a0, a1);
-            }
-          }
-          warp_store_rows(stage, packed, row ? row + c64 * 64 : nullptr, lane);
-        }
-      } else {
-        bf16* row = nullptr;
-        if (valid) {
-          const int32_t mt = args.meta[grow];
-          row = static_cast<bf16*>(args.peers.yk[mt >> 24]) + (int64_t)(mt & 0xffffff) * args.H +
-                c.nb * BN;
-        }
-#pragma unroll 1
-        for (int c64 = 0; c64 < BN / 64; ++c64) {
           uint32_t y0[32], y1[32], packed[32];
-          tmem_ld32(tbase + c64 * 64, y0);
-          tmem_ld32(tbase + c64 * 64 + 32, y1);
+          const int col = h * 128 + c64 * 64;
+          tmem_ld32(tbase + col, y0);
+          tmem_ld32(tbase + col + 32, y1);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -801,18 +621,24 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc_pair(const __grid_constan
       }
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(leader_tempty[b]);
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[b]);
     }
   }
 
   fence_before();
   __syncthreads();
-  cluster_sync();  // the pair's MMAs and remote arrivals are over before TMEM is freed
+  if (PAIR) cluster_sync();  // the pair's MMAs and remote arrivals are over before TMEM is freed
   fence_after();
-  if (wp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(TMEM_COLS)
-                 : "memory");
+  if (wp == 1) {
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(TMEM_COLS)
+                   : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(TMEM_COLS)
+                   : "memory");
+  }
   if (MODE == 1) grid_done_signal_ffn(args.done_ctr, args.peers, args.world, args.rank, args.seq);
 }
 
@@ -845,17 +671,14 @@ int tc_init() {
   const cudaError_t e =
       cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
   if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return -1;
-  if (cudaFuncSetAttribute(tc::k_ffn_tc<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::SMEM_BYTES) != cudaSuccess)
-    return -2;
-  if (cudaFuncSetAttribute(tc::k_ffn_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::SMEM_BYTES) != cudaSuccess)
-    return -2;
-  if (cudaFuncSetAttribute(tc::k_ffn_tc_pair<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::P_SMEM_BYTES) != cudaSuccess)
-    return -2;
-  if (cudaFuncSetAttribute(tc::k_ffn_tc_pair<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::P_SMEM_BYTES) != cudaSuccess)
+  if (cudaFuncSetAttribute(tc::k_ffn_tc<0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::smem_bytes<false>()) != cudaSuccess ||
+      cudaFuncSetAttribute(tc::k_ffn_tc<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::smem_bytes<false>()) != cudaSuccess ||
+      cudaFuncSetAttribute(tc::k_ffn_tc<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::smem_bytes<true>()) != cudaSuccess ||
+      cudaFuncSetAttribute(tc::k_ffn_tc<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tc::smem_bytes<true>()) != cudaSuccess)
     return -2;
   tc::g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   return 0;
@@ -869,8 +692,8 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     if (rc) return rc;
     CUtensorMap tmA1, tmB1, tmA2, tmB2;
     const uint64_t nl = (uint64_t)(a.n_local_weights > 0 ? a.n_local_weights : 1);
-    if ((rc = tc::make_tmap(&tmA1, a.recv_x, H, a.cap_rows, tc::BM))) return rc;
-    if ((rc = tc::make_tmap(&tmA2, a.act, I, a.cap_rows, tc::BM))) return rc;
+    if ((rc = tc::make_tmap(&tmA1, a.recv_x, H, a.cap_rows, 128))) return rc;
+    if ((rc = tc::make_tmap(&tmA2, a.act, I, a.cap_rows, 128))) return rc;
     if ((rc = tc::make_tmap(&tmB1, a.w_in, H, nl * 2 * I, 128))) return rc;
     if ((rc = tc::make_tmap(&tmB2, a.w_out, I, nl * H, 128))) return rc;
     tc::TcArgs g1{};
@@ -884,29 +707,26 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g1.act_ld = I;
     g1.err = a.err;
     const bool pair = !a.tc_single_cta && a.num_sms >= 2;
-    const int pair_grid = a.num_sms & ~1;
-    auto launch_pair = [&](auto kernel, const CUtensorMap& ta, const CUtensorMap& tb,
-                           const tc::TcArgs& g) -> cudaError_t {
+    // CTA pairs: 2-CTA clusters over an even grid; single CTAs: one per SM
+    auto launch = [&](auto kernel, bool as_pair, const CUtensorMap& ta, const CUtensorMap& tb,
+                      const tc::TcArgs& g) -> cudaError_t {
       cudaLaunchConfig_t cfg{};
-      cfg.gridDim = dim3((unsigned)pair_grid);
+      cfg.gridDim = dim3((unsigned)(as_pair ? (a.num_sms & ~1) : a.num_sms));
       cfg.blockDim = dim3(tc::THREADS);
-      cfg.dynamicSmemBytes = tc::P_SMEM_BYTES;
+      cfg.dynamicSmemBytes = as_pair ? tc::smem_bytes<true>() : tc::smem_bytes<false>();
       cfg.stream = st;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.x = as_pair ? 2 : 1;
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
-      cfg.numAttrs = 1;
+      cfg.numAttrs = as_pair ? 1 : 0;
       return cudaLaunchKernelEx(&cfg, kernel, ta, tb, g);
     };
-    if (pair) {
-      const cudaError_t e = launch_pair(tc::k_ffn_tc_pair<0>, tmA1, tmB1, g1);
-      if (e != cudaSuccess) return (int)e;
-    } else {
-      tc::k_ffn_tc<0><<<a.num_sms, tc::THREADS, tc::SMEM_BYTES, st>>>(tmA1, tmB1, g1);
-    }
+    cudaError_t e = pair ? launch(tc::k_ffn_tc<0, true>, true, tmA1, tmB1, g1)
+                         : launch(tc::k_ffn_tc<0, false>, false, tmA1, tmB1, g1);
+    if (e != cudaSuccess) return (int)e;
     tc::TcArgs g2{};
     g2.lay = a.layout;
     g2.K = I;
@@ -922,12 +742,9 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g2.done_ctr = a.done_ctr;
     g2.seq = a.seq;
     g2.err = a.err;
-    if (pair) {
-      const cudaError_t e = launch_pair(tc::k_ffn_tc_pair<1>, tmA2, tmB2, g2);
-      if (e != cudaSuccess) return (int)e;
-    } else {
-      tc::k_ffn_tc<1><<<a.num_sms, tc::THREADS, tc::SMEM_BYTES, st>>>(tmA2, tmB2, g2);
-    }
+    e = pair ? launch(tc::k_ffn_tc<1, true>, true, tmA2, tmB2, g2)
+             : launch(tc::k_ffn_tc<1, false>, false, tmA2, tmB2, g2);
+    if (e != cudaSuccess) return (int)e;
     return (int)cudaGetLastError();
   }
   if (H % kSimtBN != 0 || I % 32 != 0) return -3;
