@@ -38,6 +38,10 @@ __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const P
   }
 }
 
+// One warp per token: lanes s < k resolve slot s's destination row while the
+// warp loads the token's row (2 KB at a time, 64 B per lane); the row is then
+// stored once per slot. The row is read from HBM once instead of k times and
+// the metadata loads overlap the row load.
 __global__ void __launch_bounds__(256) k_dispatch(int64_t n, int topk, int row_bytes, int world,
                                                   int rank, const uint8_t* __restrict__ x,
                                                   const int64_t* __restrict__ topk_idx,
@@ -45,21 +49,47 @@ __global__ void __launch_bounds__(256) k_dispatch(int64_t n, int topk, int row_b
                                                   const int32_t* __restrict__ ent_grp,
                                                   const Layout* __restrict__ lay, PeerPtrs peers,
                                                   unsigned int* done_ctr, uint32_t seq) {
+  constexpr int VPL = 4;  // 16-byte vectors per lane per chunk
   const int lane = lane_id();
   const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
-  const int64_t m = n * topk;
   const int vec = row_bytes >> 4;
-  for (int64_t f = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); f < m; f += warps_total) {
-    const int d = ent_dest[f];
-    if (d < 0) continue;
-    const int e = (int)topk_idx[f];
-    const int off = lay->dst_off[d * kMaxExperts + e];
-    if (off < 0) continue;  // destination would overflow: error already raised
-    const int64_t pos = (int64_t)off + ent_grp[f];
-    const uint4* src = reinterpret_cast<const uint4*>(x + (f / topk) * (int64_t)row_bytes);
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peers.recv_x[d]) + pos * row_bytes);
-    for (int i = lane; i < vec; i += 32) dst[i] = __ldg(src + i);
-    if (lane == 0) peers.recv_meta[d][pos] = (rank << 24) | (int32_t)f;
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); t < n; t += warps_total) {
+    // this lane's slot (lane < topk): destination rank and row there, or -1
+    int my_d = -1;
+    int64_t my_pos = 0;
+    if (lane < topk) {
+      const int64_t f = t * topk + lane;
+      const int d = ent_dest[f];
+      if (d >= 0) {
+        const int off = lay->dst_off[d * kMaxExperts + (int)topk_idx[f]];
+        if (off >= 0) {  // a negative offset: the destination would overflow (error raised)
+          my_d = d;
+          my_pos = (int64_t)off + ent_grp[f];
+          peers.recv_meta[d][my_pos] = (rank << 24) | (int32_t)f;
+        }
+      }
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * (int64_t)row_bytes);
+    for (int c0 = 0; c0 < vec; c0 += 32 * VPL) {
+      uint4 v[VPL];
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        const int c = c0 + i * 32 + lane;
+        if (c < vec) v[i] = __ldg(src + c);
+      }
+      for (int s = 0; s < topk; ++s) {
+        const int d = __shfl_sync(0xffffffffu, my_d, s);
+        const int64_t pos = __shfl_sync(0xffffffffu, my_pos, s);
+        if (d < 0) continue;
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peers.recv_x[d]) +
+                                              pos * row_bytes);
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+          const int c = c0 + i * 32 + lane;
+          if (c < vec) dst[c] = v[i];
+        }
+      }
+    }
   }
   grid_done_signal(done_ctr, peers, world, rank, world, seq);
 }
@@ -127,19 +157,28 @@ __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); t < n; t += warps_total) {
     const bool keep = valid == nullptr || valid[t] != 0;
     float g[kMaxTopk];
-    if (keep)
-      for (int s = 0; s < topk; ++s) g[s] = Elt<T>::to_f(gate[t * topk + s]);
+#pragma unroll
+    for (int s = 0; s < kMaxTopk; ++s)
+      g[s] = (keep && s < topk) ? Elt<T>::to_f(gate[t * topk + s]) : 0.f;
+    const uint4* rows = reinterpret_cast<const uint4*>(yk + t * topk * (int64_t)H);
     for (int c = lane; c < nvec; c += 32) {
       float acc[V];
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = 0.f;
       if (keep) {
-        for (int s = 0; s < topk; ++s) {
-          const uint4 raw = reinterpret_cast<const uint4*>(yk + (t * topk + s) * (int64_t)H)[c];
-          float y[V];
-          unpack16<T>(raw, y);
+        // all of the token's slot rows in flight at once, then summed in slot order
+        uint4 raw[kMaxTopk];
 #pragma unroll
-          for (int i = 0; i < V; ++i) acc[i] += Elt<T>::round(y[i] * g[s]);
+        for (int s = 0; s < kMaxTopk; ++s)
+          if (s < topk) raw[s] = rows[(int64_t)s * nvec + c];
+#pragma unroll
+        for (int s = 0; s < kMaxTopk; ++s) {
+          if (s < topk) {
+            float y[V];
+            unpack16<T>(raw[s], y);
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] += Elt<T>::round(y[i] * g[s]);
+          }
         }
       }
       float o[V];
@@ -166,8 +205,7 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
                      const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
                      unsigned int* done_ctr, uint32_t seq, int num_sms, cudaStream_t st) {
   const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
-  const int64_t m = n * topk;
-  int64_t blocks = (m + 7) / 8;
+  int64_t blocks = (n + 7) / 8;  // 8 warps per block, one token per warp
   if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
   if (blocks < 1) blocks = 1;
   k_dispatch<<<(unsigned)blocks, 256, 0, st>>>(n, topk, row_bytes, world, rank,

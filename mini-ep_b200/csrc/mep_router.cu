@@ -67,21 +67,25 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint3
 
 // bf16 router on the warp-level tensor-core path (the router GEMM is
 // (N x H) x (H x E) with E <= 64: far too narrow for a TMEM tile to pay, and
-// the kernel is bound by reading x once from HBM). Each warp owns 16 tokens
-// and all E = 8*NT experts. H is walked in 64-column blocks; every lane loads
-// two 16-byte pieces per row and uses them for four k16 steps (the same
-// column permutation is applied to x and to the router rows, which leaves
-// every dot product unchanged).
+// the kernel is bound by reading x once from HBM). A CTA owns 16 tokens and
+// all E = 8*NT experts; its 4 warps split H into quarters (when H is a
+// multiple of 256) so that enough loads are in flight, and their partial
+// logits are added in warp order (fixed, so the result is deterministic).
+// Each warp walks its columns in 64-column blocks: every lane loads two
+// 16-byte pieces per row and uses them for four k16 steps (the same column
+// permutation is applied to x and to the router rows, which leaves every dot
+// product unchanged).
 template <int NT>
 __global__ void __launch_bounds__(128) k_router_bf16_mma(
     const bf16* __restrict__ x, const bf16* __restrict__ w, const float* __restrict__ bias,
     int64_t n, int H, int E, int k, int64_t* __restrict__ idx_out, bf16* __restrict__ gate_out,
     float* __restrict__ logits_out) {
-  __shared__ float sl[4][16][NT * 8 + 1];
+  __shared__ float part[4][16][NT * 8 + 1];
   const int wp = warp_id(), lane = lane_id();
   const int g = lane >> 2, q = lane & 3;
-  const int64_t tok0 = ((int64_t)blockIdx.x * 4 + wp) * 16;
-  if (tok0 >= n) return;
+  const int64_t tok0 = (int64_t)blockIdx.x * 16;
+  const int ksplit = (H % 256 == 0) ? 4 : 1;
+  const int kchunk = H / ksplit;
   const int64_t ra = min(tok0 + g, n - 1), rb = min(tok0 + g + 8, n - 1);
   const bf16* xa = x + ra * H + q * 16;
   const bf16* xb = x + rb * H + q * 16;
@@ -89,44 +93,51 @@ __global__ void __launch_bounds__(128) k_router_bf16_mma(
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
 
-  for (int kb = 0; kb < H; kb += 64) {
-    const uint4 alo = __ldg(reinterpret_cast<const uint4*>(xa + kb));
-    const uint4 ahi = __ldg(reinterpret_cast<const uint4*>(xa + kb + 8));
-    const uint4 blo = __ldg(reinterpret_cast<const uint4*>(xb + kb));
-    const uint4 bhi = __ldg(reinterpret_cast<const uint4*>(xb + kb + 8));
-    const uint32_t ra_lo[4] = {alo.x, alo.y, alo.z, alo.w};  // row g, columns [0,8)
-    const uint32_t ra_hi[4] = {ahi.x, ahi.y, ahi.z, ahi.w};  // row g, columns [8,16)
-    const uint32_t rb_lo[4] = {blo.x, blo.y, blo.z, blo.w};  // row g+8
-    const uint32_t rb_hi[4] = {bhi.x, bhi.y, bhi.z, bhi.w};
+  if (wp < ksplit) {
+    const int kbeg = wp * kchunk, kend = kbeg + kchunk;
+    for (int kb = kbeg; kb < kend; kb += 64) {
+      const uint4 alo = __ldg(reinterpret_cast<const uint4*>(xa + kb));
+      const uint4 ahi = __ldg(reinterpret_cast<const uint4*>(xa + kb + 8));
+      const uint4 blo = __ldg(reinterpret_cast<const uint4*>(xb + kb));
+      const uint4 bhi = __ldg(reinterpret_cast<const uint4*>(xb + kb + 8));
+      const uint32_t ra_lo[4] = {alo.x, alo.y, alo.z, alo.w};  // row g, columns [0,8)
+      const uint32_t ra_hi[4] = {ahi.x, ahi.y, ahi.z, ahi.w};  // row g, columns [8,16)
+      const uint32_t rb_lo[4] = {blo.x, blo.y, blo.z, blo.w};  // row g+8
+      const uint32_t rb_hi[4] = {bhi.x, bhi.y, bhi.z, bhi.w};
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const int ne = t * 8 + g;
-      uint4 wlo = make_uint4(0, 0, 0, 0), whi = make_uint4(0, 0, 0, 0);
-      if (ne < E) {
-        const bf16* wr = w + (int64_t)ne * H + kb + q * 16;
-        wlo = __ldg(reinterpret_cast<const uint4*>(wr));
-        whi = __ldg(reinterpret_cast<const uint4*>(wr + 8));
+      for (int t = 0; t < NT; ++t) {
+        const int ne = t * 8 + g;
+        uint4 wlo = make_uint4(0, 0, 0, 0), whi = make_uint4(0, 0, 0, 0);
+        if (ne < E) {
+          const bf16* wr = w + (int64_t)ne * H + kb + q * 16;
+          wlo = __ldg(reinterpret_cast<const uint4*>(wr));
+          whi = __ldg(reinterpret_cast<const uint4*>(wr + 8));
+        }
+        const uint32_t w_lo[4] = {wlo.x, wlo.y, wlo.z, wlo.w};
+        const uint32_t w_hi[4] = {whi.x, whi.y, whi.z, whi.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_16816(acc[t], ra_lo[j], rb_lo[j], ra_hi[j], rb_hi[j], w_lo[j], w_hi[j]);
       }
-      const uint32_t w_lo[4] = {wlo.x, wlo.y, wlo.z, wlo.w};
-      const uint32_t w_hi[4] = {whi.x, whi.y, whi.z, whi.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        mma_bf16_16816(acc[t], ra_lo[j], rb_lo[j], ra_hi[j], rb_hi[j], w_lo[j], w_hi[j]);
     }
   }
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
-    sl[wp][g][t * 8 + 2 * q] = acc[t][0];
-    sl[wp][g][t * 8 + 2 * q + 1] = acc[t][1];
-    sl[wp][g + 8][t * 8 + 2 * q] = acc[t][2];
-    sl[wp][g + 8][t * 8 + 2 * q + 1] = acc[t][3];
+    part[wp][g][t * 8 + 2 * q] = acc[t][0];
+    part[wp][g][t * 8 + 2 * q + 1] = acc[t][1];
+    part[wp][g + 8][t * 8 + 2 * q] = acc[t][2];
+    part[wp][g + 8][t * 8 + 2 * q + 1] = acc[t][3];
   }
-  __syncwarp();
-  if (lane < 16) {
+  __syncthreads();
+  if (wp == 0 && lane < 16) {
     const int64_t tok = tok0 + lane;
     if (tok < n) {
-      float* v = sl[wp][lane];
-      for (int e = 0; e < E; ++e) v[e] = logit_to_model<bf16>(v[e], bias, e);
+      float* v = part[0][lane];
+      for (int e = 0; e < E; ++e) {
+        float sum = v[e];
+        for (int w2 = 1; w2 < ksplit; ++w2) sum += part[w2][lane][e];
+        v[e] = logit_to_model<bf16>(sum, bias, e);
+      }
       if (logits_out)
         for (int e = 0; e < E; ++e) logits_out[tok * E + e] = v[e];
       select_topk<bf16>(v, E, k, tok, idx_out, gate_out);
@@ -168,7 +179,7 @@ void launch_router(int dtype, const void* x, const void* router_w, const float* 
                    float* logits_out, cudaStream_t st) {
   if (n <= 0) return;
   if (dtype == kBF16 && hidden % 64 == 0 && experts % 8 == 0 && experts <= 64) {
-    const unsigned grid = (unsigned)((n + 63) / 64);
+    const unsigned grid = (unsigned)((n + 15) / 16);
     auto xb = static_cast<const bf16*>(x);
     auto wb = static_cast<const bf16*>(router_w);
     auto gb = static_cast<bf16*>(gate_out);
