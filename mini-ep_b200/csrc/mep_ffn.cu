@@ -327,8 +327,11 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         : "memory");
   }
 }
+// "accumulator drained" arrival: relaxed, because it only releases TMEM
+// (ordered by tcgen05.fence::before_thread_sync), not the epilogue's global
+// stores, which must not be waited for here
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
                : "memory");
 }
 __device__ __forceinline__ void fence_before() {
@@ -579,10 +582,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
       if (!ok) break;
       fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
+      // drain this warp's TMEM columns into registers, hand the accumulator
+      // back to the MMA warp, then store
+      uint32_t packed[2][32];
       if (MODE == 0) {
         // act columns [h*64, h*64+64) of this tile: gate at TMEM columns
         // h*64.., up at 128 + h*64..
-        uint32_t packed[32];
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t g[32], u[32];
@@ -592,36 +597,40 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            packed[half * 16 + i] =
+            packed[0][half * 16 + i] =
                 pack_bf16x2(swiglu_bf16(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i])),
                             swiglu_bf16(__uint_as_float(g[2 * i + 1]), __uint_as_float(u[2 * i + 1])));
         }
-        bf16* row = valid ? args.act + grow * args.act_ld + c.nb * 128 + h * 64 : nullptr;
-        warp_store_rows(stage, packed, row, lane);
       } else {
         // output columns [h*128, h*128+128) of this tile, 64 at a time
-        bf16* row = valid ? static_cast<bf16*>(args.peers.yk[mt >> 24]) +
-                                (int64_t)(mt & 0xffffff) * args.H + c.nb * BN + h * 128
-                          : nullptr;
-#pragma unroll 1
+#pragma unroll
         for (int c64 = 0; c64 < 2; ++c64) {
-          uint32_t y0[32], y1[32], packed[32];
+          uint32_t y0[32], y1[32];
           const int col = h * 128 + c64 * 64;
           tmem_ld32(tbase + col, y0);
           tmem_ld32(tbase + col + 32, y1);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            packed[i] = pack_bf16x2(__uint_as_float(y0[2 * i]), __uint_as_float(y0[2 * i + 1]));
-            packed[16 + i] =
+            packed[c64][i] = pack_bf16x2(__uint_as_float(y0[2 * i]), __uint_as_float(y0[2 * i + 1]));
+            packed[c64][16 + i] =
                 pack_bf16x2(__uint_as_float(y1[2 * i]), __uint_as_float(y1[2 * i + 1]));
           }
-          warp_store_rows(stage, packed, row ? row + c64 * 64 : nullptr, lane);
         }
       }
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[b]);
+      if (MODE == 0) {
+        bf16* row = valid ? args.act + grow * args.act_ld + c.nb * 128 + h * 64 : nullptr;
+        warp_store_rows(stage, packed[0], row, lane);
+      } else {
+        bf16* row = valid ? static_cast<bf16*>(args.peers.yk[mt >> 24]) +
+                                (int64_t)(mt & 0xffffff) * args.H + c.nb * BN + h * 128
+                          : nullptr;
+        warp_store_rows(stage, packed[0], row, lane);
+        warp_store_rows(stage, packed[1], row ? row + 64 : nullptr, lane);
+      }
     }
   }
 

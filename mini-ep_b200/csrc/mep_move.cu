@@ -140,7 +140,7 @@ __device__ __forceinline__ uint4 pack16<bf16>(const float (&o)[8]) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <typename T>
+template <typename T, int KMAX>
 __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int world,
                                                  const T* __restrict__ yk,
                                                  const T* __restrict__ gate,
@@ -156,9 +156,9 @@ __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int
   const int nvec = H / V;
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); t < n; t += warps_total) {
     const bool keep = valid == nullptr || valid[t] != 0;
-    float g[kMaxTopk];
+    float g[KMAX];
 #pragma unroll
-    for (int s = 0; s < kMaxTopk; ++s)
+    for (int s = 0; s < KMAX; ++s)
       g[s] = (keep && s < topk) ? Elt<T>::to_f(gate[t * topk + s]) : 0.f;
     const uint4* rows = reinterpret_cast<const uint4*>(yk + t * topk * (int64_t)H);
     for (int c = lane; c < nvec; c += 32) {
@@ -167,12 +167,12 @@ __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int
       for (int i = 0; i < V; ++i) acc[i] = 0.f;
       if (keep) {
         // all of the token's slot rows in flight at once, then summed in slot order
-        uint4 raw[kMaxTopk];
+        uint4 raw[KMAX];
 #pragma unroll
-        for (int s = 0; s < kMaxTopk; ++s)
+        for (int s = 0; s < KMAX; ++s)
           if (s < topk) raw[s] = rows[(int64_t)s * nvec + c];
 #pragma unroll
-        for (int s = 0; s < kMaxTopk; ++s) {
+        for (int s = 0; s < KMAX; ++s) {
           if (s < topk) {
             float y[V];
             unpack16<T>(raw[s], y);
@@ -225,18 +225,24 @@ void launch_combine(int dtype, int64_t n, int topk, int hidden, int world, const
   int64_t blocks = (n + 7) / 8;
   if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
   if (blocks < 1) blocks = 1;
-  if (dtype == kBF16)
-    k_combine<bf16><<<(unsigned)blocks, 256, 0, st>>>(
-        n, topk, hidden, world, static_cast<const bf16*>(yk_local),
-        static_cast<const bf16*>(topk_gate), valid, static_cast<const bf16*>(h),
-        residual_multiplier, static_cast<bf16*>(out), static_cast<bf16*>(h_out), flags_local, seq,
-        wc);
-  else
-    k_combine<float><<<(unsigned)blocks, 256, 0, st>>>(
-        n, topk, hidden, world, static_cast<const float*>(yk_local),
-        static_cast<const float*>(topk_gate), valid, static_cast<const float*>(h),
-        residual_multiplier, static_cast<float*>(out), static_cast<float*>(h_out), flags_local,
-        seq, wc);
+  // slot rows in flight per lane: sized to top-k (8 or 16) to keep registers low
+#define MEP_COMBINE(T, KM)                                                                  \
+  k_combine<T, KM><<<(unsigned)blocks, 256, 0, st>>>(                                       \
+      n, topk, hidden, world, static_cast<const T*>(yk_local), static_cast<const T*>(topk_gate), \
+      valid, static_cast<const T*>(h), residual_multiplier, static_cast<T*>(out),             \
+      static_cast<T*>(h_out), flags_local, seq, wc)
+  if (dtype == kBF16) {
+    if (topk <= 8)
+      MEP_COMBINE(bf16, 8);
+    else
+      MEP_COMBINE(bf16, kMaxTopk);
+  } else {
+    if (topk <= 8)
+      MEP_COMBINE(float, 8);
+    else
+      MEP_COMBINE(float, kMaxTopk);
+  }
+#undef MEP_COMBINE
 }
 
 }  // namespace mep
