@@ -31,9 +31,9 @@ using bf16 = __nv_bfloat16;
 
 __device__ __forceinline__ void grid_done_signal_ffn(unsigned int* done_ctr, const PeerPtrs& peers,
                                                      int world, int rank, uint32_t seq) {
-  __threadfence_system();
-  __syncthreads();
+  __syncthreads();  // this CTA's stores happen before thread 0's fence below
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned prev = atomicAdd(done_ctr, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();

@@ -26,9 +26,9 @@ using bf16 = __nv_bfloat16;
 // [flag_base + rank] on each peer is raised to `seq` by the last CTA to finish.
 __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const PeerPtrs& peers,
                                                  int world, int rank, int flag_base, uint32_t seq) {
-  __threadfence_system();
-  __syncthreads();
+  __syncthreads();  // this CTA's stores happen before thread 0's fence below
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned prev = atomicAdd(done_ctr, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();
@@ -38,10 +38,12 @@ __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const P
   }
 }
 
-// One warp per token: lanes s < k resolve slot s's destination row while the
-// warp loads the token's row (2 KB at a time, 64 B per lane); the row is then
-// stored once per slot. The row is read from HBM once instead of k times and
-// the metadata loads overlap the row load.
+// One warp per token pair: lanes 0-15 resolve the destination rows of token
+// t's slots and lanes 16-31 those of token t + stride, while the warp loads
+// both tokens' rows (2 KB at a time, 64 B per lane per token); each row is
+// then stored once per slot. A row is read from HBM once instead of k times,
+// the metadata loads overlap the row loads, and two rows are in flight per
+// warp.
 __global__ void __launch_bounds__(256) k_dispatch(int64_t n, int topk, int row_bytes, int world,
                                                   int rank, const uint8_t* __restrict__ x,
                                                   const int64_t* __restrict__ topk_idx,
@@ -51,42 +53,54 @@ __global__ void __launch_bounds__(256) k_dispatch(int64_t n, int topk, int row_b
                                                   unsigned int* done_ctr, uint32_t seq) {
   constexpr int VPL = 4;  // 16-byte vectors per lane per chunk
   const int lane = lane_id();
-  const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int vec = row_bytes >> 4;
-  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); t < n; t += warps_total) {
-    // this lane's slot (lane < topk): destination rank and row there, or -1
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); t < n; t += 2 * stride) {
+    const int64_t tt[2] = {t, t + stride};
+    // this lane's slot: token tt[lane / 16], slot lane % 16
     int my_d = -1;
     int64_t my_pos = 0;
-    if (lane < topk) {
-      const int64_t f = t * topk + lane;
-      const int d = ent_dest[f];
-      if (d >= 0) {
-        const int off = lay->dst_off[d * kMaxExperts + (int)topk_idx[f]];
-        if (off >= 0) {  // a negative offset: the destination would overflow (error raised)
-          my_d = d;
-          my_pos = (int64_t)off + ent_grp[f];
-          peers.recv_meta[d][my_pos] = (rank << 24) | (int32_t)f;
+    {
+      const int64_t tok = tt[lane >> 4];
+      const int slot = lane & 15;
+      if (tok < n && slot < topk) {
+        const int64_t f = tok * topk + slot;
+        const int d = ent_dest[f];
+        if (d >= 0) {
+          const int off = lay->dst_off[d * kMaxExperts + (int)topk_idx[f]];
+          if (off >= 0) {  // a negative offset: the destination would overflow (error raised)
+            my_d = d;
+            my_pos = (int64_t)off + ent_grp[f];
+            peers.recv_meta[d][my_pos] = (rank << 24) | (int32_t)f;
+          }
         }
       }
     }
-    const uint4* src = reinterpret_cast<const uint4*>(x + t * (int64_t)row_bytes);
     for (int c0 = 0; c0 < vec; c0 += 32 * VPL) {
-      uint4 v[VPL];
+      uint4 v[2][VPL];
 #pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        const int c = c0 + i * 32 + lane;
-        if (c < vec) v[i] = __ldg(src + c);
-      }
-      for (int s = 0; s < topk; ++s) {
-        const int d = __shfl_sync(0xffffffffu, my_d, s);
-        const int64_t pos = __shfl_sync(0xffffffffu, my_pos, s);
-        if (d < 0) continue;
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peers.recv_x[d]) +
-                                              pos * row_bytes);
+      for (int u = 0; u < 2; ++u) {
+        if (tt[u] >= n) continue;
+        const uint4* src = reinterpret_cast<const uint4*>(x + tt[u] * (int64_t)row_bytes);
 #pragma unroll
         for (int i = 0; i < VPL; ++i) {
           const int c = c0 + i * 32 + lane;
-          if (c < vec) dst[c] = v[i];
+          if (c < vec) v[u][i] = __ldg(src + c);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        for (int s = 0; s < topk; ++s) {
+          const int d = __shfl_sync(0xffffffffu, my_d, u * 16 + s);
+          const int64_t pos = __shfl_sync(0xffffffffu, my_pos, u * 16 + s);
+          if (d < 0) continue;
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peers.recv_x[d]) +
+                                                pos * row_bytes);
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) {
+            const int c = c0 + i * 32 + lane;
+            if (c < vec) dst[c] = v[u][i];
+          }
         }
       }
     }
@@ -140,6 +154,32 @@ __device__ __forceinline__ uint4 pack16<bf16>(const float (&o)[8]) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// acc += model_dtype(y * g), element-wise over one 16-byte vector. For bf16
+// the products are taken two at a time with bf16x2 multiplies, which round
+// the exact product to bf16 exactly as multiplying in fp32 and rounding does
+// (a product of two bf16 values is exact in fp32).
+template <typename T>
+__device__ __forceinline__ void add_gated(float (&acc)[Vec16<T>::N], const uint4& raw, float g);
+template <>
+__device__ __forceinline__ void add_gated<float>(float (&acc)[4], const uint4& raw, float g) {
+  acc[0] += __uint_as_float(raw.x) * g;
+  acc[1] += __uint_as_float(raw.y) * g;
+  acc[2] += __uint_as_float(raw.z) * g;
+  acc[3] += __uint_as_float(raw.w) * g;
+}
+template <>
+__device__ __forceinline__ void add_gated<bf16>(float (&acc)[8], const uint4& raw, float g) {
+  const __nv_bfloat162 g2 = __float2bfloat162_rn(g);  // g is a bf16 value: exact
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 p = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]), g2);
+    const float2 f = __bfloat1622float2(p);
+    acc[2 * i] += f.x;
+    acc[2 * i + 1] += f.y;
+  }
+}
+
 template <typename T, int KMAX>
 __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int world,
                                                  const T* __restrict__ yk,
@@ -173,12 +213,7 @@ __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int
           if (s < topk) raw[s] = rows[(int64_t)s * nvec + c];
 #pragma unroll
         for (int s = 0; s < KMAX; ++s) {
-          if (s < topk) {
-            float y[V];
-            unpack16<T>(raw[s], y);
-#pragma unroll
-            for (int i = 0; i < V; ++i) acc[i] += Elt<T>::round(y[i] * g[s]);
-          }
+          if (s < topk) add_gated<T>(acc, raw[s], g[s]);
         }
       }
       float o[V];
@@ -205,7 +240,7 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
                      const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
                      unsigned int* done_ctr, uint32_t seq, int num_sms, cudaStream_t st) {
   const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
-  int64_t blocks = (n + 7) / 8;  // 8 warps per block, one token per warp
+  int64_t blocks = (n + 15) / 16;  // 8 warps per block, two tokens per warp
   if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
   if (blocks < 1) blocks = 1;
   k_dispatch<<<(unsigned)blocks, 256, 0, st>>>(n, topk, row_bytes, world, rank,

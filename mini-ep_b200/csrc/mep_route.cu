@@ -71,13 +71,24 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_rank(
   __shared__ int rr_mod[kMaxExperts];
   const int wp = warp_id(), lane = lane_id();
   const int chunk = blockIdx.x;
+  // prefix of the earlier chunks' histograms: the block's threads split the
+  // chunks (thread i sums chunks i / E, i / E + parts, ...), then add up
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int b = 0;
-    for (int c = 0; c < chunk; ++c) b += chunk_hist[(int64_t)c * E + e];
-    base[e] = b;
+    base[e] = 0;
     rr_mod[e] = (int)(rr[e] % nrep[e]);
-    for (int w = 0; w < kRouteWarps; ++w) wcnt[w][e] = 0;
   }
+  __syncthreads();
+  {
+    const int parts = blockDim.x / E > 0 ? blockDim.x / E : 1;
+    for (int i = threadIdx.x; i < parts * E; i += blockDim.x) {
+      const int e = i % E, part = i / E;
+      int b = 0;
+      for (int c = part; c < chunk; c += parts) b += chunk_hist[(int64_t)c * E + e];
+      if (b) atomicAdd(&base[e], b);  // integer sums: the order does not matter
+    }
+  }
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    for (int w = 0; w < kRouteWarps; ++w) wcnt[w][e] = 0;
   __syncthreads();
   // this warp's entries: tokens [t0, t0+32) -> flat entries [t0*k, (t0+32)*k)
   const int64_t t0 = (int64_t)chunk * kRouteChunkTokens + wp * 32;
@@ -158,7 +169,8 @@ __global__ void __launch_bounds__(256) k_route_finalize(
     int32_t* dst = peers.cnt_in[d] + (int64_t)rank * world * E;
     for (int i = threadIdx.x; i < world * E; i += blockDim.x) dst[i] = cnt[i];
   }
-  __threadfence_system();
+  __syncthreads();  // every thread's count stores happen before the fence below
+  if (threadIdx.x == 0) __threadfence_system();
   __syncthreads();
   if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, seq);
 }

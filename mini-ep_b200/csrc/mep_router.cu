@@ -48,6 +48,50 @@ __device__ __forceinline__ void select_topk(const float* v, int E, int k, int64_
   }
 }
 
+// Warp-parallel top-k for one token: lane l holds the model-dtype logits of
+// experts l and l+32 (-inf past E). k rounds of a 5-step shuffle argmax
+// (larger value first, lower index on ties, as the serial rule); lanes < k
+// write the result. E <= 64.
+template <typename T>
+__device__ __forceinline__ void select_topk_warp(float v0, float v1, int k, int64_t tok,
+                                                 int64_t* idx_out, T* gate_out) {
+  const int lane = lane_id();
+  float my_v = 0.f, top0 = 0.f;
+  int my_i = 0;
+  float ex_sum = 0.f;
+  for (int i = 0; i < k; ++i) {
+    // this lane's best remaining candidate
+    float bv = v0;
+    int bi = lane;
+    if (v1 > bv) {
+      bv = v1;
+      bi = lane + 32;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (bi == lane) v0 = -INFINITY;
+    if (bi == lane + 32) v1 = -INFINITY;
+    if (i == 0) top0 = bv;
+    const float e = expf(bv - top0);
+    ex_sum += e;
+    if (lane == i) {
+      my_v = e;
+      my_i = bi;
+    }
+  }
+  if (lane < k) {
+    idx_out[tok * k + lane] = my_i;
+    gate_out[tok * k + lane] = Elt<T>::from_f(my_v * (1.f / ex_sum));
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ float logit_to_model(float acc, const float* bias, int e) {
   float l = Elt<T>::round(acc);
@@ -129,19 +173,24 @@ __global__ void __launch_bounds__(128) k_router_bf16_mma(
     part[wp][g + 8][t * 8 + 2 * q + 1] = acc[t][3];
   }
   __syncthreads();
-  if (wp == 0 && lane < 16) {
-    const int64_t tok = tok0 + lane;
-    if (tok < n) {
-      float* v = part[0][lane];
-      for (int e = 0; e < E; ++e) {
-        float sum = v[e];
-        for (int w2 = 1; w2 < ksplit; ++w2) sum += part[w2][lane][e];
-        v[e] = logit_to_model<bf16>(sum, bias, e);
+  // each warp selects for 4 of the 16 tokens, one expert per lane (two for E > 32)
+  for (int r = wp * 4; r < wp * 4 + 4; ++r) {
+    const int64_t tok = tok0 + r;
+    if (tok >= n) break;
+    float v[2];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int e = lane + 32 * h2;
+      if (e < E) {
+        float sum = part[0][r][e];
+        for (int w2 = 1; w2 < ksplit; ++w2) sum += part[w2][r][e];
+        v[h2] = logit_to_model<bf16>(sum, bias, e);
+        if (logits_out) logits_out[tok * E + e] = v[h2];
+      } else {
+        v[h2] = -INFINITY;
       }
-      if (logits_out)
-        for (int e = 0; e < E; ++e) logits_out[tok * E + e] = v[e];
-      select_topk<bf16>(v, E, k, tok, idx_out, gate_out);
     }
+    select_topk_warp<bf16>(v[0], v[1], k, tok, idx_out, gate_out);
   }
 }
 
