@@ -36,7 +36,7 @@ struct mep_ctx {
   unsigned int* done_ctr = nullptr;   // [0] dispatch, [1] expert FFN
   int* err_host = nullptr;
   int* err_dev = nullptr;
-  uint32_t seq = 0;
+  uint32_t* seq = nullptr;  // device: sequence number of the current layer step
   unsigned long long timeout_ns = 10ull * 1000 * 1000 * 1000;
   int force_simt = 0;
   int tc_single_cta = 0;
@@ -208,6 +208,7 @@ int mep_ctx_create(int rank, int world, int device, int num_layers, int num_expe
       {reinterpret_cast<void**>(&c->route_counts), (size_t)num_layers * num_experts * 8},
       {reinterpret_cast<void**>(&c->recv_per_layer), (size_t)num_layers * 8},
       {reinterpret_cast<void**>(&c->done_ctr), 2 * sizeof(unsigned int)},
+      {reinterpret_cast<void**>(&c->seq), sizeof(uint32_t)},
   };
   for (auto& a : allocs) {
     e = cudaMalloc(a.p, a.bytes);
@@ -235,9 +236,9 @@ int mep_ctx_destroy(mep_ctx* c) {
   cudaDeviceSynchronize();
   for (int r = 0; r < kMaxWorld; ++r)
     if (c->peer_open[r] && c->peer_base[r]) cudaIpcCloseMemHandle(c->peer_base[r]);
-  void* ptrs[] = {c->sym,    c->act,        c->chunk_hist,   c->ent_dest,       c->ent_grp,
-                  c->my_counts, c->layout,  c->owners,       c->nrep,           c->rr,
-                  c->route_counts, c->recv_per_layer, c->done_ctr};
+  void* ptrs[] = {c->sym,      c->act,    c->chunk_hist, c->ent_dest,     c->ent_grp,
+                  c->my_counts, c->layout, c->owners,     c->nrep,         c->rr,
+                  c->route_counts, c->recv_per_layer, c->done_ctr, c->seq};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (c->err_host) cudaFreeHost(c->err_host);
@@ -355,7 +356,6 @@ int mep_route(mep_ctx* c, int layer, const int64_t* topk_idx, const uint8_t* val
                     std::to_string(c->n_local_l[layer]) + " experts resident on this rank)");
   if (int rc = check_peers(c)) return rc;
   if (int rc = use_device(c)) return rc;
-  c->seq += 1;
   c->cur_layer = layer;
   c->cur_n = n;
   launch_route(n, c->k, c->E, c->world, c->rank, topk_idx, valid, owners_of(c, layer),
@@ -384,7 +384,7 @@ int mep_dispatch(mep_ctx* c, const void* x, const int64_t* topk_idx, int64_t n, 
                   as_stream(stream));
   // the stage ends when every rank's rows for this rank have landed
   launch_wait_flags(reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->world, c->world,
-                    c->seq, kErrWaitData, wait_cfg(c), as_stream(stream));
+                    c->seq, 0u, kErrWaitData, wait_cfg(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   c->stage = 2;
   return MEP_OK;
@@ -551,8 +551,8 @@ int mep_debug_wait(mep_ctx* c, uint32_t target, int64_t timeout_ms, void* stream
   if (timeout_ms < 1) return fail(c, MEP_ERR_INVALID, "timeout_ms must be >= 1");
   if (int rc = use_device(c)) return rc;
   WaitCfg wc{c->err_dev, (unsigned long long)timeout_ms * 1000000ull};
-  launch_wait_flags(reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), 0, 1, target,
-                    kErrWaitDebug, wc, as_stream(stream));
+  launch_wait_flags(reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), 0, 1, nullptr,
+                    target, kErrWaitDebug, wc, as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   return MEP_OK;
 }

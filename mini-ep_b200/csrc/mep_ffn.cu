@@ -30,14 +30,15 @@ namespace {
 using bf16 = __nv_bfloat16;
 
 __device__ __forceinline__ void grid_done_signal_ffn(unsigned int* done_ctr, const PeerPtrs& peers,
-                                                     int world, int rank, uint32_t seq) {
+                                                     int world, int rank, const uint32_t* seq) {
   __syncthreads();  // this CTA's stores happen before thread 0's fence below
   if (threadIdx.x == 0) {
     __threadfence_system();
     const unsigned prev = atomicAdd(done_ctr, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();
-      for (int d = 0; d < world; ++d) st_release_sys(peers.flags[d] + 2 * world + rank, seq);
+      const uint32_t step = *seq;
+      for (int d = 0; d < world; ++d) st_release_sys(peers.flags[d] + 2 * world + rank, step);
       *done_ctr = 0u;
     }
   }
@@ -90,7 +91,7 @@ __global__ void __launch_bounds__(256) k_ffn_simt(const T* __restrict__ A, int l
                                                   T* __restrict__ act, int act_ld,
                                                   const int32_t* __restrict__ meta, PeerPtrs peers,
                                                   int H, int world, int rank,
-                                                  unsigned int* done_ctr, uint32_t seq) {
+                                                  unsigned int* done_ctr, const uint32_t* seq) {
   __shared__ float As[kSimtBK][kSimtBM + 4];
   __shared__ float Bs[kSimtBK][kSimtBN + 4];
   __shared__ float Cs[kSimtBM][kSimtBN + 1];
@@ -201,11 +202,11 @@ struct Smem {
 // epilogue staging: 32 rows x 128 B per warp, 16-byte chunks XOR-swizzled by row
 constexpr int STAGE_WARP_BYTES = 32 * 128;
 template <bool PAIR>
-constexpr int off_stage() {
+__host__ __device__ constexpr int off_stage() {
   return Geo<PAIR>::DATA + (((int)sizeof(Smem<PAIR>) + 127) / 128) * 128;
 }
 template <bool PAIR>
-constexpr int smem_bytes() {
+__host__ __device__ constexpr int smem_bytes() {
   return off_stage<PAIR>() + EPI_WARPS * STAGE_WARP_BYTES + 1024;
 }
 static_assert(smem_bytes<false>() <= 232448, "single-CTA kernel exceeds shared memory");
@@ -410,7 +411,7 @@ struct TcArgs {
   PeerPtrs peers;
   int H, world, rank;
   unsigned int* done_ctr;
-  uint32_t seq;
+  const uint32_t* seq;
   int* err;
 };
 

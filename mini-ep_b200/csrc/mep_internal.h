@@ -68,7 +68,7 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,
                   int64_t* route_counts_l, int32_t* chunk_hist, int32_t* ent_dest,
                   int32_t* ent_grp, int32_t* my_counts, const PeerPtrs& peers,
-                  uint32_t seq, WaitCfg wc, cudaStream_t st);
+                  uint32_t* seq, WaitCfg wc, cudaStream_t st);
 
 void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids,
                       const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,
@@ -78,21 +78,22 @@ void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids,
 void launch_layout(int world, int rank, int experts, const int32_t* owners_l,
                    const int32_t* nrep_l, const int32_t* cnt_in_local,
                    const uint32_t* flags_local, int64_t* recv_per_layer_l, int64_t cap_rows,
-                   Layout* layout, uint32_t seq, WaitCfg wc, cudaStream_t st);
+                   Layout* layout, const uint32_t* seq, WaitCfg wc, cudaStream_t st);
 
 // ---------------------------------------------------------------- movement
 void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int rank,
                      const void* x, const int64_t* topk_idx, const int32_t* ent_dest,
                      const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
-                     unsigned int* done_ctr, uint32_t seq, int num_sms, cudaStream_t st);
+                     unsigned int* done_ctr, const uint32_t* seq, int num_sms, cudaStream_t st);
 
-void launch_wait_flags(const uint32_t* flags_local, int first, int world, uint32_t seq,
-                       int errcode, WaitCfg wc, cudaStream_t st);
+// waits for flags [first, first + world) to reach *seq (or `target` when seq is null)
+void launch_wait_flags(const uint32_t* flags_local, int first, int world, const uint32_t* seq,
+                       uint32_t target, int errcode, WaitCfg wc, cudaStream_t st);
 
 void launch_combine(int dtype, int64_t n, int topk, int hidden, int world,
                     const void* yk_local, const void* topk_gate, const uint8_t* valid,
                     const void* h, float residual_multiplier, void* out, void* h_out,
-                    const uint32_t* flags_local, uint32_t seq, WaitCfg wc, int num_sms,
+                    const uint32_t* flags_local, const uint32_t* seq, WaitCfg wc, int num_sms,
                     cudaStream_t st);
 
 // ---------------------------------------------------------------- expert FFN
@@ -108,7 +109,7 @@ struct FfnArgs {
   const Layout* layout;
   PeerPtrs peers;
   unsigned int* done_ctr;
-  uint32_t seq;
+  const uint32_t* seq;      // device: sequence number of the current layer step
   int num_sms;
   int force_simt;           // 1: run the CUDA-core kernels even for bf16
   int tc_single_cta;        // 1: one CTA per 128x256 tile instead of CTA pairs per 256x256

@@ -25,14 +25,16 @@ using bf16 = __nv_bfloat16;
 // Signal "this kernel's stores are done" to every rank: flag slot
 // [flag_base + rank] on each peer is raised to `seq` by the last CTA to finish.
 __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const PeerPtrs& peers,
-                                                 int world, int rank, int flag_base, uint32_t seq) {
+                                                 int world, int rank, int flag_base,
+                                                 const uint32_t* seq) {
   __syncthreads();  // this CTA's stores happen before thread 0's fence below
   if (threadIdx.x == 0) {
     __threadfence_system();
     const unsigned prev = atomicAdd(done_ctr, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();
-      for (int d = 0; d < world; ++d) st_release_sys(peers.flags[d] + flag_base + rank, seq);
+      const uint32_t step = *seq;
+      for (int d = 0; d < world; ++d) st_release_sys(peers.flags[d] + flag_base + rank, step);
       *done_ctr = 0u;
     }
   }
@@ -50,7 +52,7 @@ __global__ void __launch_bounds__(256) k_dispatch(int64_t n, int topk, int row_b
                                                   const int32_t* __restrict__ ent_dest,
                                                   const int32_t* __restrict__ ent_grp,
                                                   const Layout* __restrict__ lay, PeerPtrs peers,
-                                                  unsigned int* done_ctr, uint32_t seq) {
+                                                  unsigned int* done_ctr, const uint32_t* seq) {
   constexpr int VPL = 4;  // 16-byte vectors per lane per chunk
   const int lane = lane_id();
   const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -108,9 +110,10 @@ __global__ void __launch_bounds__(256) k_dispatch(int64_t n, int topk, int row_b
   grid_done_signal(done_ctr, peers, world, rank, world, seq);
 }
 
-__global__ void k_wait_flags(const uint32_t* flags, int first, int world, uint32_t seq, int code,
-                             WaitCfg wc) {
-  if (threadIdx.x < world) wait_flag(flags + first + threadIdx.x, seq, code, wc);
+__global__ void k_wait_flags(const uint32_t* flags, int first, int world, const uint32_t* seq,
+                             uint32_t target, int code, WaitCfg wc) {
+  const uint32_t step = seq ? *seq : target;
+  if (threadIdx.x < world) wait_flag(flags + first + threadIdx.x, step, code, wc);
 }
 
 template <typename T>
@@ -187,9 +190,10 @@ __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int
                                                  const uint8_t* __restrict__ valid,
                                                  const T* __restrict__ h, float rm,
                                                  T* __restrict__ out, T* __restrict__ h_out,
-                                                 const uint32_t* flags, uint32_t seq, WaitCfg wc) {
+                                                 const uint32_t* flags, const uint32_t* seq,
+                                                 WaitCfg wc) {
   constexpr int V = Vec16<T>::N;
-  if (threadIdx.x < world) wait_flag(flags + 2 * world + threadIdx.x, seq, kErrWaitDone, wc);
+  if (threadIdx.x < world) wait_flag(flags + 2 * world + threadIdx.x, *seq, kErrWaitDone, wc);
   __syncthreads();
   const int lane = lane_id();
   const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -238,7 +242,8 @@ __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int
 void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int rank,
                      const void* x, const int64_t* topk_idx, const int32_t* ent_dest,
                      const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
-                     unsigned int* done_ctr, uint32_t seq, int num_sms, cudaStream_t st) {
+                     unsigned int* done_ctr, const uint32_t* seq, int num_sms,
+                     cudaStream_t st) {
   const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
   int64_t blocks = (n + 15) / 16;  // 8 warps per block, two tokens per warp
   if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
@@ -248,15 +253,15 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
                                                ent_grp, layout, peers, done_ctr, seq);
 }
 
-void launch_wait_flags(const uint32_t* flags_local, int first, int world, uint32_t seq,
-                       int errcode, WaitCfg wc, cudaStream_t st) {
-  k_wait_flags<<<1, 32, 0, st>>>(flags_local, first, world, seq, errcode, wc);
+void launch_wait_flags(const uint32_t* flags_local, int first, int world, const uint32_t* seq,
+                       uint32_t target, int errcode, WaitCfg wc, cudaStream_t st) {
+  k_wait_flags<<<1, 32, 0, st>>>(flags_local, first, world, seq, target, errcode, wc);
 }
 
 void launch_combine(int dtype, int64_t n, int topk, int hidden, int world, const void* yk_local,
                     const void* topk_gate, const uint8_t* valid, const void* h,
                     float residual_multiplier, void* out, void* h_out, const uint32_t* flags_local,
-                    uint32_t seq, WaitCfg wc, int num_sms, cudaStream_t st) {
+                    const uint32_t* seq, WaitCfg wc, int num_sms, cudaStream_t st) {
   int64_t blocks = (n + 7) / 8;
   if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
   if (blocks < 1) blocks = 1;

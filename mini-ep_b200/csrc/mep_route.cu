@@ -140,8 +140,11 @@ __global__ void __launch_bounds__(256) k_route_finalize(
     int nchunks, int E, int world, int rank, const int32_t* __restrict__ owners,
     const int32_t* __restrict__ nrep, int64_t* __restrict__ rr, int64_t* __restrict__ route_counts,
     const int32_t* __restrict__ chunk_hist, int32_t* __restrict__ my_counts, PeerPtrs peers,
-    uint32_t seq, int publish) {
+    uint32_t* seq, int publish) {
   __shared__ int cnt[kMaxWorld * kMaxExperts];
+  // this layer step's sequence number: one past the previous step's (kept on
+  // the device so that a captured graph of the step stays valid on replay)
+  const uint32_t step = publish ? *seq + 1u : 0u;
   __shared__ int any_rep;
   if (threadIdx.x == 0) any_rep = 0;
   for (int i = threadIdx.x; i < world * E; i += blockDim.x) cnt[i] = 0;
@@ -172,7 +175,9 @@ __global__ void __launch_bounds__(256) k_route_finalize(
   __syncthreads();  // every thread's count stores happen before the fence below
   if (threadIdx.x == 0) __threadfence_system();
   __syncthreads();
-  if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, seq);
+  if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, step);
+  __syncthreads();
+  if (threadIdx.x == 0) *seq = step;
 }
 
 __global__ void k_dest_to_i64(int64_t m, const int32_t* __restrict__ d, int64_t* __restrict__ out) {
@@ -188,13 +193,14 @@ __global__ void __launch_bounds__(256) k_layout(int world, int rank, int E,
                                                 const uint32_t* __restrict__ flags,
                                                 int64_t* __restrict__ recv_per_layer,
                                                 int64_t cap_rows, Layout* __restrict__ lay,
-                                                uint32_t seq, WaitCfg wc) {
+                                                const uint32_t* seq, WaitCfg wc) {
+  const uint32_t step = *seq;
   __shared__ int R[kMaxWorld][kMaxExperts];       // rows per (dest, expert)
   __shared__ int before[kMaxWorld][kMaxExperts];  // rows from sources < rank
   __shared__ int seg[kMaxWorld][kMaxExperts];
   __shared__ unsigned char res[kMaxWorld][kMaxExperts];
   __shared__ int overflow[kMaxWorld];
-  if (threadIdx.x < world) wait_flag(flags + threadIdx.x, seq, kErrWaitCounts, wc);
+  if (threadIdx.x < world) wait_flag(flags + threadIdx.x, step, kErrWaitCounts, wc);
   __syncthreads();
   for (int i = threadIdx.x; i < world * E; i += blockDim.x) {
     const int d = i / E, e = i % E;
@@ -256,7 +262,7 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   const int64_t* topk_idx, const uint8_t* valid, const int32_t* owners_l,
                   const int32_t* nrep_l, int64_t* rr_l, int64_t* route_counts_l,
                   int32_t* chunk_hist, int32_t* ent_dest, int32_t* ent_grp, int32_t* my_counts,
-                  const PeerPtrs& peers, uint32_t seq, WaitCfg wc, cudaStream_t st) {
+                  const PeerPtrs& peers, uint32_t* seq, WaitCfg wc, cudaStream_t st) {
   const int nchunks = (int)((n + kRouteChunkTokens - 1) / kRouteChunkTokens);
   if (nchunks > 0) {
     k_route_hist<<<nchunks, kRouteThreads, 0, st>>>(n, topk, experts, topk_idx, valid, chunk_hist,
@@ -282,12 +288,12 @@ void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids, const i
   }
   PeerPtrs none{};
   k_route_finalize<<<1, 256, 0, st>>>(nchunks, experts, kMaxWorld, 0, owners_l, nrep_l, rr_l,
-                                      nullptr, chunk_hist, my_counts, none, 0, 0);
+                                      nullptr, chunk_hist, my_counts, none, nullptr, 0);
 }
 
 void launch_layout(int world, int rank, int experts, const int32_t* owners_l,
                    const int32_t* nrep_l, const int32_t* cnt_in_local, const uint32_t* flags_local,
-                   int64_t* recv_per_layer_l, int64_t cap_rows, Layout* layout, uint32_t seq,
+                   int64_t* recv_per_layer_l, int64_t cap_rows, Layout* layout, const uint32_t* seq,
                    WaitCfg wc, cudaStream_t st) {
   k_layout<<<1, 256, 0, st>>>(world, rank, experts, owners_l, nrep_l, cnt_in_local, flags_local,
                               recv_per_layer_l, cap_rows, layout, seq, wc);

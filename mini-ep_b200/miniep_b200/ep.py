@@ -368,6 +368,63 @@ class EPMoEBackend:
         return h_out.view_as(h), idx, gate
 
 
+class GraphedMoEBlock:
+    """The MoE half of ``Block.forward`` (router + expert-parallel layer +
+    residual, miniep/modeling.py:192-197) for a fixed token count, captured once
+    into a CUDA graph over static device buffers and replayed per step: one
+    launch per layer step instead of ten, no host work in between.
+
+    The step's sequence number lives on the device, so replays stay in lockstep
+    with the other ranks exactly like eager calls. Every rank must construct
+    its GraphedMoEBlock at the same point (construction runs one warm-up step)
+    and then replay the same number of times.
+    """
+
+    def __init__(self, backend: "EPMoEBackend", n_tokens: int, router_w,
+                 residual_multiplier: float, bias=None):
+        comm = backend.comm
+        self.backend, self.n = backend, n_tokens
+        dev = backend.w_in.device
+        H, k = comm.hidden, comm.topk
+        self.x = torch.zeros(n_tokens, H, dtype=comm.dtype, device=dev)
+        self.h = torch.zeros(n_tokens, H, dtype=comm.dtype, device=dev)
+        self.h_out = torch.empty_like(self.h)
+        self.idx = torch.empty(n_tokens, k, dtype=torch.int64, device=dev)
+        self.gate = torch.empty(n_tokens, k, dtype=comm.dtype, device=dev)
+        self.router_w = router_w.to(comm.dtype).contiguous()
+        self.bias = None if bias is None else bias.to(device=dev, dtype=torch.float32).contiguous()
+        self.rm = float(residual_multiplier)
+        self.n_local = backend._prepare(self.x)
+        self._step()  # warm-up outside capture (resolves driver entry points, kernel attributes)
+        torch.cuda.current_stream().synchronize()
+        comm.check()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+
+    def _step(self):
+        be, comm = self.backend, self.backend.comm
+        L, ctx, st, n = _lib.lib(), comm._ctx, _stream(), self.n
+        check(L.mep_router_topk(ctx, ptr(self.x), ptr(self.router_w), ptr(self.bias), n,
+                                ptr(self.idx), ptr(self.gate), None, st), ctx, "mep_router_topk")
+        check(L.mep_route(ctx, be.layer, ptr(self.idx), None, n, self.n_local, st), ctx, "mep_route")
+        check(L.mep_dispatch(ctx, ptr(self.x), ptr(self.idx), n, st), ctx, "mep_dispatch")
+        check(L.mep_expert_ffn(ctx, ptr(be.w_in), ptr(be.w_out), self.n_local, st), ctx,
+              "mep_expert_ffn")
+        check(L.mep_combine(ctx, ptr(self.gate), None, n, ptr(self.h), self.rm, None,
+                            ptr(self.h_out), st), ctx, "mep_combine")
+
+    def __call__(self, x=None, h=None):
+        """Copy x / h (device or pinned host tensors) into the static inputs
+        when given, replay the step, return the static output h + moe(x) * rm."""
+        if x is not None:
+            self.x.copy_(x, non_blocking=True)
+        if h is not None:
+            self.h.copy_(h, non_blocking=True)
+        self.graph.replay()
+        return self.h_out
+
+
 def router_topk(comm: Comm, x_flat, router_w, bias=None, return_logits: bool = False):
     """Router of ``Block.forward`` (miniep/modeling.py:193-195) on the device:
     (topk_idx int64, topk_gate model dtype[, logits fp32])."""
