@@ -313,3 +313,22 @@ def test_argument_errors():
     be.local_experts = [0, 1]
     with pytest.raises(MEPError, match="local_experts"):
         be(lb.x.cuda(), idx[:8], torch.zeros(8, 8, dtype=torch.bfloat16, device="cuda"))
+
+
+def test_graphed_block_replays_match_eager_calls():
+    from miniep_b200 import GraphedMoEBlock
+    sh = synth.SHAPES["a"]
+    n = 512
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], 2 * n, seed=9,
+                          dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0].cuda()
+    hs = synth.make_tokens(2 * n, sh["hidden"], seed=10, dtype=torch.bfloat16).cuda()
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
+    router = lb.router.cuda()
+    blk = GraphedMoEBlock(be, n, router, synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
+    for part in (0, 1, 0):
+        x, h = lb.x[part * n:(part + 1) * n].cuda(), hs[part * n:(part + 1) * n]
+        got = blk(x, h).clone()
+        want, _, _ = be.moe_block(h, x, router, synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
+        assert torch.equal(got, want)
+    be.comm.check()
