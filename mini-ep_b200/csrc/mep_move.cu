@@ -245,7 +245,9 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
                      unsigned int* done_ctr, const uint32_t* seq, int num_sms,
                      cudaStream_t st) {
   const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
-  int64_t blocks = (n + 15) / 16;  // 8 warps per block, two tokens per warp
+  // 8 warps per block: one warp per token up to the grid cap; a warp takes a
+  // second token (t + stride) only when the cap is reached
+  int64_t blocks = (n + 7) / 8;
   if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
   if (blocks < 1) blocks = 1;
   k_dispatch<<<(unsigned)blocks, 256, 0, st>>>(n, topk, row_bytes, world, rank,
