@@ -67,7 +67,7 @@ def config(a, sh) -> dict:
     return {"workload": workload_name(a), "tokens_per_step": a.tokens, "hidden": sh["hidden"],
             "experts": sh["experts"], "topk": sh["topk"], "inter": sh["inter"],
             "router": "zipf(1.2) bias x2.0, layer 0", "placement": a.plan,
-            "l2": "flushed between timed steps (512 MiB write, outside the step events)"}
+            "l2": "flushed between timed steps (512 MiB write + 256 MiB read, outside the step events)"}
 
 
 # ------------------------------------------------------------------- clocks
@@ -248,7 +248,14 @@ def main_b200(a):
     gate = torch.empty(n, k, dtype=torch.bfloat16, device=dev)
     h_out = torch.empty_like(h)
     P = _lib.ptr
+    # L2 flush between steps: write 512 MiB, then read 256 MiB so that the
+    # written lines are evicted (written back) before the step, not during it
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush_rd = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+
+    def flush_l2():
+        flush.zero_()
+        flush_rd.sum()
 
     def eager_step(st, ev_ffn=None):
         # mep_moe_block's sequence, with events around the expert FFN stage
@@ -271,7 +278,7 @@ def main_b200(a):
             dist.barrier()
         torch.cuda.synchronize()
         for i in range(steps):
-            flush.zero_()
+            flush_l2()
             if world > 1:
                 dist.barrier()
             starts[i].record()
