@@ -40,72 +40,73 @@ __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const P
   }
 }
 
-// One warp per token pair: lanes 0-15 resolve the destination rows of token
-// t's slots and lanes 16-31 those of token t + stride, while the warp loads
-// both tokens' rows (2 KB at a time, 64 B per lane per token); each row is
-// then stored once per slot. A row is read from HBM once instead of k times,
-// the metadata loads overlap the row loads, and two rows are in flight per
-// warp.
-__global__ void __launch_bounds__(256) k_dispatch(int64_t n, int topk, int row_bytes, int world,
-                                                  int rank, const uint8_t* __restrict__ x,
-                                                  const int64_t* __restrict__ topk_idx,
-                                                  const int32_t* __restrict__ ent_dest,
-                                                  const int32_t* __restrict__ ent_grp,
-                                                  const Layout* __restrict__ lay, PeerPtrs peers,
-                                                  unsigned int* done_ctr, const uint32_t* seq) {
-  constexpr int VPL = 4;  // 16-byte vectors per lane per chunk
-  const int lane = lane_id();
-  const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
+// Dispatch, one warp per token: lanes s < k resolve slot s's destination row
+// (and store the 4-byte tag there) while the warp loads the token's row into
+// one of its shared-memory row buffers; lane 0 then issues one bulk copy
+// (cp.async.bulk, shared -> global, the TMA engine) per slot into the
+// destination rank's receive buffer. The copies run asynchronously, many per
+// SM, which keeps NVLink busy far better than stores issued by the warps
+// themselves; a row buffer is reused only once its earlier copies have read
+// it. The row is read from HBM once instead of k times.
+constexpr int kDispatchWarps = 4;
+constexpr int kDispatchBufs = 3;  // row buffers per warp
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
+    int64_t n, int topk, int row_bytes, int world, int rank, const uint8_t* __restrict__ x,
+    const int64_t* __restrict__ topk_idx, const int32_t* __restrict__ ent_dest,
+    const int32_t* __restrict__ ent_grp, const Layout* __restrict__ lay, PeerPtrs peers,
+    unsigned int* done_ctr, const uint32_t* seq) {
+  extern __shared__ __align__(128) uint8_t dsmem[];
+  const int lane = lane_id(), wp = warp_id();
+  uint8_t* bufs = dsmem + (size_t)wp * kDispatchBufs * row_bytes;
+  const int64_t stride = (int64_t)gridDim.x * kDispatchWarps;
   const int vec = row_bytes >> 4;
-  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); t < n; t += 2 * stride) {
-    const int64_t tt[2] = {t, t + stride};
-    // this lane's slot: token tt[lane / 16], slot lane % 16
+  int buf = 0;
+  for (int64_t t = (int64_t)blockIdx.x * kDispatchWarps + wp; t < n; t += stride) {
     int my_d = -1;
     int64_t my_pos = 0;
-    {
-      const int64_t tok = tt[lane >> 4];
-      const int slot = lane & 15;
-      if (tok < n && slot < topk) {
-        const int64_t f = tok * topk + slot;
-        const int d = ent_dest[f];
-        if (d >= 0) {
-          const int off = lay->dst_off[d * kMaxExperts + (int)topk_idx[f]];
-          if (off >= 0) {  // a negative offset: the destination would overflow (error raised)
-            my_d = d;
-            my_pos = (int64_t)off + ent_grp[f];
-            peers.recv_meta[d][my_pos] = (rank << 24) | (int32_t)f;
-          }
+    if (lane < topk) {
+      const int64_t f = t * topk + lane;
+      const int d = ent_dest[f];
+      if (d >= 0) {
+        const int off = lay->dst_off[d * kMaxExperts + (int)topk_idx[f]];
+        if (off >= 0) {  // a negative offset: the destination would overflow (error raised)
+          my_d = d;
+          my_pos = (int64_t)off + ent_grp[f];
+          peers.recv_meta[d][my_pos] = (rank << 24) | (int32_t)f;
         }
       }
     }
-    for (int c0 = 0; c0 < vec; c0 += 32 * VPL) {
-      uint4 v[2][VPL];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        if (tt[u] >= n) continue;
-        const uint4* src = reinterpret_cast<const uint4*>(x + tt[u] * (int64_t)row_bytes);
-#pragma unroll
-        for (int i = 0; i < VPL; ++i) {
-          const int c = c0 + i * 32 + lane;
-          if (c < vec) v[u][i] = __ldg(src + c);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        for (int s = 0; s < topk; ++s) {
-          const int d = __shfl_sync(0xffffffffu, my_d, u * 16 + s);
-          const int64_t pos = __shfl_sync(0xffffffffu, my_pos, u * 16 + s);
-          if (d < 0) continue;
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peers.recv_x[d]) +
-                                                pos * row_bytes);
-#pragma unroll
-          for (int i = 0; i < VPL; ++i) {
-            const int c = c0 + i * 32 + lane;
-            if (c < vec) dst[c] = v[u][i];
-          }
-        }
+    uint8_t* row = bufs + (size_t)buf * row_bytes;
+    // the buffer's previous copies (issued kDispatchBufs tokens ago) must have read it
+    if (lane == 0)
+      asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kDispatchBufs - 1) : "memory");
+    __syncwarp();
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * (int64_t)row_bytes);
+    for (int c = lane; c < vec; c += 32) reinterpret_cast<uint4*>(row)[c] = __ldg(src + c);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // smem writes -> bulk copies
+    __syncwarp();
+    for (int s = 0; s < topk; ++s) {
+      const int d = __shfl_sync(0xffffffffu, my_d, s);
+      const int64_t pos = __shfl_sync(0xffffffffu, my_pos, s);
+      if (lane == 0 && d >= 0) {
+        uint8_t* dst = static_cast<uint8_t*>(peers.recv_x[d]) + pos * row_bytes;
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                     "r"(smem_addr(row)), "r"(row_bytes)
+                     : "memory");
       }
     }
+    if (lane == 0) asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    buf = buf + 1 == kDispatchBufs ? 0 : buf + 1;
+  }
+  // every copy of this warp has completed (written) before the completion signal
+  if (lane == 0) {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
   }
   grid_done_signal(done_ctr, peers, world, rank, world, seq);
 }
@@ -245,14 +246,19 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
                      unsigned int* done_ctr, const uint32_t* seq, int num_sms,
                      cudaStream_t st) {
   const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
-  // 8 warps per block: one warp per token up to the grid cap; a warp takes a
-  // second token (t + stride) only when the cap is reached
-  int64_t blocks = (n + 7) / 8;
-  if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
+  const size_t smem = (size_t)kDispatchWarps * kDispatchBufs * row_bytes;
+  static size_t smem_set = 0;
+  if (smem > 48 * 1024 && smem > smem_set) {
+    cudaFuncSetAttribute(k_dispatch, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    smem_set = smem;
+  }
+  // one warp per token up to the grid cap
+  int64_t blocks = (n + kDispatchWarps - 1) / kDispatchWarps;
+  if (blocks > (int64_t)num_sms * 16) blocks = (int64_t)num_sms * 16;
   if (blocks < 1) blocks = 1;
-  k_dispatch<<<(unsigned)blocks, 256, 0, st>>>(n, topk, row_bytes, world, rank,
-                                               static_cast<const uint8_t*>(x), topk_idx, ent_dest,
-                                               ent_grp, layout, peers, done_ctr, seq);
+  k_dispatch<<<(unsigned)blocks, 32 * kDispatchWarps, smem, st>>>(
+      n, topk, row_bytes, world, rank, static_cast<const uint8_t*>(x), topk_idx, ent_dest, ent_grp,
+      layout, peers, done_ctr, seq);
 }
 
 void launch_wait_flags(const uint32_t* flags_local, int first, int world, const uint32_t* seq,
