@@ -15,9 +15,10 @@ struct mep_ctx {
   int64_t max_tokens = 0, cap_rows = 0;
   int num_sms = 0;
   size_t elt = 4;
-  // symmetric region (exported over CUDA IPC): flags | counts | meta | recv_x | yk
+  // symmetric region (exported over CUDA IPC): flags | counts | meta | land | yk
   uint8_t* sym = nullptr;
-  size_t sym_bytes = 0, off_flags = 0, off_cnt = 0, off_meta = 0, off_recvx = 0, off_yk = 0;
+  size_t sym_bytes = 0, off_flags = 0, off_cnt = 0, off_meta = 0, off_land = 0, off_yk = 0;
+  void* recv_x = nullptr;  // expert-grouped receive rows (local only)
   uint8_t* peer_base[kMaxWorld] = {};
   bool peer_open[kMaxWorld] = {};
   PeerPtrs peers{};
@@ -73,7 +74,8 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 void build_peers(mep_ctx* c) {
   for (int r = 0; r < kMaxWorld; ++r) {
     uint8_t* b = r < c->world ? c->peer_base[r] : nullptr;
-    c->peers.recv_x[r] = b ? b + c->off_recvx : nullptr;
+    c->peers.land[r] = b ? b + c->off_land : nullptr;
+    c->peers.recv_x[r] = r == c->rank ? c->recv_x : nullptr;  // only this rank's rows are stored here
     c->peers.recv_meta[r] = b ? reinterpret_cast<int32_t*>(b + c->off_meta) : nullptr;
     c->peers.yk[r] = b ? b + c->off_yk : nullptr;
     c->peers.cnt_in[r] = b ? reinterpret_cast<int32_t*>(b + c->off_cnt) : nullptr;
@@ -183,8 +185,8 @@ int mep_ctx_create(int rank, int world, int device, int num_layers, int num_expe
   off = align_up(off + (size_t)kMaxWorld * kMaxWorld * kMaxExperts * sizeof(int32_t), 1024);
   c->off_meta = off;
   off = align_up(off + (size_t)c->cap_rows * sizeof(int32_t), 1024);
-  c->off_recvx = off;
-  off = align_up(off + (size_t)c->cap_rows * hidden * elt, 1024);
+  c->off_land = off;  // [src rank][max_tokens][H]: each token row once per destination rank
+  off = align_up(off + (size_t)(world > 1 ? world : 0) * max_tokens * hidden * elt, 1024);
   c->off_yk = off;
   off = align_up(off + (size_t)max_tokens * topk * hidden * elt, 1024);
   c->sym_bytes = off;
@@ -197,6 +199,7 @@ int mep_ctx_create(int rank, int world, int device, int num_layers, int num_expe
   } allocs[] = {
       {reinterpret_cast<void**>(&c->sym), c->sym_bytes},
       {&c->act, (size_t)c->cap_rows * inter * elt},
+      {&c->recv_x, (size_t)c->cap_rows * hidden * elt},
       {reinterpret_cast<void**>(&c->chunk_hist), (size_t)nchunks * num_experts * 4},
       {reinterpret_cast<void**>(&c->ent_dest), (size_t)max_entries * 4},
       {reinterpret_cast<void**>(&c->ent_grp), (size_t)max_entries * 4},
@@ -236,7 +239,7 @@ int mep_ctx_destroy(mep_ctx* c) {
   cudaDeviceSynchronize();
   for (int r = 0; r < kMaxWorld; ++r)
     if (c->peer_open[r] && c->peer_base[r]) cudaIpcCloseMemHandle(c->peer_base[r]);
-  void* ptrs[] = {c->sym,      c->act,    c->chunk_hist, c->ent_dest,     c->ent_grp,
+  void* ptrs[] = {c->sym,      c->act,    c->recv_x,     c->chunk_hist,   c->ent_dest,     c->ent_grp,
                   c->my_counts, c->layout, c->owners,     c->nrep,         c->rr,
                   c->route_counts, c->recv_per_layer, c->done_ctr, c->seq};
   for (void* p : ptrs)
@@ -379,12 +382,18 @@ int mep_dispatch(mep_ctx* c, const void* x, const int64_t* topk_idx, int64_t n, 
                 reinterpret_cast<const uint32_t*>(c->sym + c->off_flags),
                 c->recv_per_layer + layer, c->cap_rows, c->layout, c->seq, wait_cfg(c),
                 as_stream(stream));
-  launch_dispatch(c->dtype, n, c->k, c->H, c->world, c->rank, x, topk_idx, c->ent_dest,
+  launch_dispatch(c->dtype, n, c->k, c->H, c->world, c->rank, c->max_tokens,
+                  x, topk_idx, c->ent_dest,
                   c->ent_grp, c->layout, c->peers, c->done_ctr, c->seq, c->num_sms,
                   as_stream(stream));
-  // the stage ends when every rank's rows for this rank have landed
+  // the stage ends when every rank's rows for this rank have landed and sit in
+  // their expert-segment rows
   launch_wait_flags(reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->world, c->world,
                     c->seq, 0u, kErrWaitData, wait_cfg(c), as_stream(stream));
+  if (c->world > 1)
+    launch_fanout(c->dtype, c->H, c->k, c->rank, c->max_tokens, c->layout,
+                  reinterpret_cast<const int32_t*>(c->sym + c->off_meta), c->sym + c->off_land,
+                  c->recv_x, c->num_sms, as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   c->stage = 2;
   return MEP_OK;
@@ -404,7 +413,7 @@ int mep_expert_ffn(mep_ctx* c, const void* w_in, const void* w_out, int n_local,
   a.world = c->world;
   a.rank = c->rank;
   a.cap_rows = c->cap_rows;
-  a.recv_x = c->sym + c->off_recvx;
+  a.recv_x = c->recv_x;
   a.recv_meta = reinterpret_cast<const int32_t*>(c->sym + c->off_meta);
   a.act = c->act;
   a.w_in = w_in;

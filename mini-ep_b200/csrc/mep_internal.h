@@ -45,7 +45,8 @@ struct Layout {
 
 // Pointers every rank can reach (own and peers' symmetric buffers).
 struct PeerPtrs {
-  void* recv_x[kMaxWorld];
+  void* recv_x[kMaxWorld];     // expert-grouped receive rows
+  void* land[kMaxWorld];       // token landing buffers: [src rank][max_tokens][H]
   int32_t* recv_meta[kMaxWorld];
   void* yk[kMaxWorld];
   int32_t* cnt_in[kMaxWorld];
@@ -82,11 +83,18 @@ void launch_layout(int world, int rank, int experts, const int32_t* owners_l,
 
 // ---------------------------------------------------------------- movement
 void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int rank,
+                     int64_t max_tokens,
                      const void* x, const int64_t* topk_idx, const int32_t* ent_dest,
                      const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
                      unsigned int* done_ctr, const uint32_t* seq, int num_sms, cudaStream_t st);
 
 // waits for flags [first, first + world) to reach *seq (or `target` when seq is null)
+// Receive rows that came from other ranks: copy each from the landing
+// buffer (row [src][token]) to its expert-segment row.
+void launch_fanout(int dtype, int hidden, int topk, int rank, int64_t max_tokens,
+                   const Layout* layout, const int32_t* recv_meta, const void* land,
+                   void* recv_x, int num_sms, cudaStream_t st);
+
 void launch_wait_flags(const uint32_t* flags_local, int first, int world, const uint32_t* seq,
                        uint32_t target, int errcode, WaitCfg wc, cudaStream_t st);
 

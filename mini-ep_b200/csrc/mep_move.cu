@@ -41,13 +41,15 @@ __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const P
 }
 
 // Dispatch, one warp per token: lanes s < k resolve slot s's destination row
-// (and store the 4-byte tag there) while the warp loads the token's row into
-// one of its shared-memory row buffers; lane 0 then issues one bulk copy
-// (cp.async.bulk, shared -> global, the TMA engine) per slot into the
-// destination rank's receive buffer. The copies run asynchronously, many per
-// SM, which keeps NVLink busy far better than stores issued by the warps
-// themselves; a row buffer is reused only once its earlier copies have read
-// it. The row is read from HBM once instead of k times.
+// in the destination's expert-grouped layout and store the 4-byte tag there
+// (source rank, flat entry index). The warp loads the token's row into one of
+// its shared-memory row buffers and lane 0 issues bulk copies (cp.async.bulk,
+// shared -> global, the TMA engine): one per slot that stays on this rank,
+// straight into its receive row, and ONE per distinct remote destination rank
+// into that rank's landing buffer [this rank][token], however many of the
+// token's slots go there (the receiver fans it out locally). The copies run
+// asynchronously; a row buffer is reused only once its earlier copies have
+// read it.
 constexpr int kDispatchWarps = 4;
 constexpr int kDispatchBufs = 3;  // row buffers per warp
 
@@ -56,10 +58,10 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 }
 
 __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
-    int64_t n, int topk, int row_bytes, int world, int rank, const uint8_t* __restrict__ x,
-    const int64_t* __restrict__ topk_idx, const int32_t* __restrict__ ent_dest,
-    const int32_t* __restrict__ ent_grp, const Layout* __restrict__ lay, PeerPtrs peers,
-    unsigned int* done_ctr, const uint32_t* seq) {
+    int64_t n, int topk, int row_bytes, int world, int rank, int64_t max_tokens,
+    const uint8_t* __restrict__ x, const int64_t* __restrict__ topk_idx,
+    const int32_t* __restrict__ ent_dest, const int32_t* __restrict__ ent_grp,
+    const Layout* __restrict__ lay, PeerPtrs peers, unsigned int* done_ctr, const uint32_t* seq) {
   extern __shared__ __align__(128) uint8_t dsmem[];
   const int lane = lane_id(), wp = warp_id();
   uint8_t* bufs = dsmem + (size_t)wp * kDispatchBufs * row_bytes;
@@ -81,6 +83,15 @@ __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
         }
       }
     }
+    // local slots each need their own row; a remote rank needs the row once
+    bool first_remote = my_d >= 0 && my_d != rank;
+    for (int j = 0; j < topk; ++j) {
+      const int dj = __shfl_sync(0xffffffffu, my_d, j);
+      if (j < lane && dj == my_d) first_remote = false;
+    }
+    const unsigned remote = __ballot_sync(0xffffffffu, first_remote);
+    const unsigned local = __ballot_sync(0xffffffffu, my_d == rank);
+    if ((remote | local) == 0u) continue;
     uint8_t* row = bufs + (size_t)buf * row_bytes;
     // the buffer's previous copies (issued kDispatchBufs tokens ago) must have read it
     if (lane == 0)
@@ -93,12 +104,15 @@ __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
     for (int s = 0; s < topk; ++s) {
       const int d = __shfl_sync(0xffffffffu, my_d, s);
       const int64_t pos = __shfl_sync(0xffffffffu, my_pos, s);
-      if (lane == 0 && d >= 0) {
-        uint8_t* dst = static_cast<uint8_t*>(peers.recv_x[d]) + pos * row_bytes;
+      uint8_t* dst = nullptr;
+      if ((local >> s) & 1u)
+        dst = static_cast<uint8_t*>(peers.recv_x[rank]) + pos * row_bytes;
+      else if ((remote >> s) & 1u)
+        dst = static_cast<uint8_t*>(peers.land[d]) + ((int64_t)rank * max_tokens + t) * row_bytes;
+      if (lane == 0 && dst)
         asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
                      "r"(smem_addr(row)), "r"(row_bytes)
                      : "memory");
-      }
     }
     if (lane == 0) asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     buf = buf + 1 == kDispatchBufs ? 0 : buf + 1;
@@ -109,6 +123,41 @@ __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
     asm volatile("fence.proxy.async.global;" ::: "memory");
   }
   grid_done_signal(done_ctr, peers, world, rank, world, seq);
+}
+
+// Fan-out on the receiver: every receive row whose tag names another rank is
+// copied from that rank's landing row [src][token] (one warp per row).
+__global__ void __launch_bounds__(256) k_fanout(int row_bytes, int topk, int rank,
+                                                int64_t max_tokens, const Layout* __restrict__ lay,
+                                                const int32_t* __restrict__ meta,
+                                                const uint8_t* __restrict__ land,
+                                                uint8_t* __restrict__ recv_x) {
+  __shared__ int s_prefix[kMaxExperts + 1], s_base[kMaxExperts], s_rows[kMaxExperts];
+  const int nl = lay->n_local;
+  for (int i = threadIdx.x; i <= nl; i += blockDim.x) s_prefix[i] = lay->tile_prefix[i];
+  for (int i = threadIdx.x; i < nl; i += blockDim.x) {
+    s_base[i] = lay->seg_base[i];
+    s_rows[i] = lay->seg_rows[i];
+  }
+  __syncthreads();
+  const int64_t total = (int64_t)lay->total_mtiles * kRowAlign;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int lane = lane_id(), vec = row_bytes >> 4;
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); w < total; w += warps) {
+    const int tile = (int)(w / kRowAlign);
+    int j = 0;
+    while (j + 1 < nl && s_prefix[j + 1] <= tile) ++j;
+    const int local = (tile - s_prefix[j]) * kRowAlign + (int)(w % kRowAlign);
+    if (local >= s_rows[j]) continue;
+    const int64_t p = (int64_t)s_base[j] + local;
+    const int32_t mt = meta[p];
+    const int src = mt >> 24;
+    if (src == rank) continue;
+    const int64_t t = (mt & 0xffffff) / topk;
+    const uint4* from = reinterpret_cast<const uint4*>(land + ((int64_t)src * max_tokens + t) * row_bytes);
+    uint4* to = reinterpret_cast<uint4*>(recv_x + p * row_bytes);
+    for (int c = lane; c < vec; c += 32) to[c] = from[c];
+  }
 }
 
 __global__ void k_wait_flags(const uint32_t* flags, int first, int world, const uint32_t* seq,
@@ -241,10 +290,10 @@ __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int
 }  // namespace
 
 void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int rank,
-                     const void* x, const int64_t* topk_idx, const int32_t* ent_dest,
-                     const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
-                     unsigned int* done_ctr, const uint32_t* seq, int num_sms,
-                     cudaStream_t st) {
+                     int64_t max_tokens, const void* x, const int64_t* topk_idx,
+                     const int32_t* ent_dest, const int32_t* ent_grp, const Layout* layout,
+                     const PeerPtrs& peers, unsigned int* done_ctr, const uint32_t* seq,
+                     int num_sms, cudaStream_t st) {
   const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
   const size_t smem = (size_t)kDispatchWarps * kDispatchBufs * row_bytes;
   static size_t smem_set = 0;
@@ -257,8 +306,17 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
   if (blocks > (int64_t)num_sms * 16) blocks = (int64_t)num_sms * 16;
   if (blocks < 1) blocks = 1;
   k_dispatch<<<(unsigned)blocks, 32 * kDispatchWarps, smem, st>>>(
-      n, topk, row_bytes, world, rank, static_cast<const uint8_t*>(x), topk_idx, ent_dest, ent_grp,
-      layout, peers, done_ctr, seq);
+      n, topk, row_bytes, world, rank, max_tokens, static_cast<const uint8_t*>(x), topk_idx,
+      ent_dest, ent_grp, layout, peers, done_ctr, seq);
+}
+
+void launch_fanout(int dtype, int hidden, int topk, int rank, int64_t max_tokens,
+                   const Layout* layout, const int32_t* recv_meta, const void* land, void* recv_x,
+                   int num_sms, cudaStream_t st) {
+  k_fanout<<<(unsigned)num_sms * 8, 256, 0, st>>>(hidden * (dtype == kBF16 ? 2 : 4), topk, rank,
+                                                  max_tokens, layout, recv_meta,
+                                                  static_cast<const uint8_t*>(land),
+                                                  static_cast<uint8_t*>(recv_x));
 }
 
 void launch_wait_flags(const uint32_t* flags_local, int first, int world, const uint32_t* seq,
