@@ -34,7 +34,7 @@ struct mep_ctx {
   int64_t* rr = nullptr;      // [L][E]
   int64_t* route_counts = nullptr;    // [L][E]
   int64_t* recv_per_layer = nullptr;  // [L]
-  unsigned int* done_ctr = nullptr;   // [0] dispatch, [1] expert FFN
+  unsigned int* done_ctr = nullptr;   // [0] dispatch, [1] expert FFN, [2..3] routing grid barrier
   int* err_host = nullptr;
   int* err_dev = nullptr;
   uint32_t* seq = nullptr;  // device: sequence number of the current layer step
@@ -210,7 +210,7 @@ int mep_ctx_create(int rank, int world, int device, int num_layers, int num_expe
       {reinterpret_cast<void**>(&c->rr), (size_t)num_layers * num_experts * 8},
       {reinterpret_cast<void**>(&c->route_counts), (size_t)num_layers * num_experts * 8},
       {reinterpret_cast<void**>(&c->recv_per_layer), (size_t)num_layers * 8},
-      {reinterpret_cast<void**>(&c->done_ctr), 2 * sizeof(unsigned int)},
+      {reinterpret_cast<void**>(&c->done_ctr), 4 * sizeof(unsigned int)},
       {reinterpret_cast<void**>(&c->seq), sizeof(uint32_t)},
   };
   for (auto& a : allocs) {
@@ -342,7 +342,7 @@ int mep_router_topk(mep_ctx* c, const void* x, const void* router_w, const float
     return fail(c, MEP_ERR_INVALID, "NULL argument");
   if (int rc = use_device(c)) return rc;
   launch_router(c->dtype, x, router_w, bias, n, c->H, c->E, c->k, topk_idx_out, topk_gate_out,
-                logits_out, as_stream(stream));
+                logits_out, c->num_sms, c->err_dev, as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   return MEP_OK;
 }
@@ -364,7 +364,8 @@ int mep_route(mep_ctx* c, int layer, const int64_t* topk_idx, const uint8_t* val
   launch_route(n, c->k, c->E, c->world, c->rank, topk_idx, valid, owners_of(c, layer),
                nrep_of(c, layer), c->rr + (int64_t)layer * c->E,
                c->route_counts + (int64_t)layer * c->E, c->chunk_hist, c->ent_dest, c->ent_grp,
-               c->my_counts, c->peers, c->seq, wait_cfg(c), as_stream(stream));
+               c->my_counts, c->peers, c->seq, c->done_ctr + 2, c->num_sms, wait_cfg(c),
+               as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   c->stage = 1;
   return MEP_OK;

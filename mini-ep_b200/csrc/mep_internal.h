@@ -61,7 +61,7 @@ struct WaitCfg {
 // ---------------------------------------------------------------- router
 void launch_router(int dtype, const void* x, const void* router_w, const float* bias,
                    int64_t n, int hidden, int experts, int topk, int64_t* idx_out,
-                   void* gate_out, float* logits_out, cudaStream_t st);
+                   void* gate_out, float* logits_out, int num_sms, int* err, cudaStream_t st);
 
 // ---------------------------------------------------------------- routing
 void launch_route(int64_t n, int topk, int experts, int world, int rank,
@@ -69,7 +69,7 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,
                   int64_t* route_counts_l, int32_t* chunk_hist, int32_t* ent_dest,
                   int32_t* ent_grp, int32_t* my_counts, const PeerPtrs& peers,
-                  uint32_t* seq, WaitCfg wc, cudaStream_t st);
+                  uint32_t* seq, unsigned int* sync, int num_sms, WaitCfg wc, cudaStream_t st);
 
 void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids,
                       const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,

@@ -53,9 +53,6 @@ __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const P
 constexpr int kDispatchWarps = 4;
 constexpr int kDispatchBufs = 3;  // row buffers per warp
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
 
 __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
     int64_t n, int topk, int row_bytes, int world, int rank, int64_t max_tokens,
@@ -111,7 +108,7 @@ __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
         dst = static_cast<uint8_t*>(peers.land[d]) + ((int64_t)rank * max_tokens + t) * row_bytes;
       if (lane == 0 && dst)
         asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
-                     "r"(smem_addr(row)), "r"(row_bytes)
+                     "r"(smem_u32(row)), "r"(row_bytes)
                      : "memory");
     }
     if (lane == 0) asm volatile("cp.async.bulk.commit_group;" ::: "memory");
@@ -259,8 +256,11 @@ __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int
       float acc[V];
 #pragma unroll
       for (int i = 0; i < V; ++i) acc[i] = 0.f;
+      // the residual row and all of the token's slot rows in flight at once,
+      // then the slots summed in slot order
+      uint4 hr = make_uint4(0, 0, 0, 0);
+      if (h_out) hr = reinterpret_cast<const uint4*>(h + t * (int64_t)H)[c];
       if (keep) {
-        // all of the token's slot rows in flight at once, then summed in slot order
         uint4 raw[KMAX];
 #pragma unroll
         for (int s = 0; s < KMAX; ++s)
@@ -275,7 +275,6 @@ __global__ void __launch_bounds__(256) k_combine(int64_t n, int topk, int H, int
       for (int i = 0; i < V; ++i) o[i] = Elt<T>::round(acc[i]);
       if (out) reinterpret_cast<uint4*>(out + t * (int64_t)H)[c] = pack16<T>(o);
       if (h_out) {
-        const uint4 hr = reinterpret_cast<const uint4*>(h + t * (int64_t)H)[c];
         float hv[V];
         unpack16<T>(hr, hv);
         float r[V];

@@ -180,6 +180,189 @@ __global__ void __launch_bounds__(256) k_route_finalize(
   if (threadIdx.x == 0) *seq = step;
 }
 
+// ---------------------------------------------------------------------------
+// The three routing passes above as ONE launch, for the layer step.
+//
+// grid G <= number of SMs (one 256-thread CTA per SM at most, so every CTA of
+// the grid is resident at once); CTA b owns tokens [b*tpc, (b+1)*tpc), tpc a
+// multiple of 256. Phase 1: every CTA reads the round-robin state, counts its
+// kept entries per expert into chunk_hist[b] and arrives at a grid barrier
+// (bounded wait). Phase 2: CTA 0 does the finalize work (totals, per-(dest,
+// expert) counts, rr update after every CTA has read rr, stats, publish);
+// every CTA then ranks its entries, 256 tokens per round, exactly as
+// k_route_rank does for a chunk.
+struct RouteSync {
+  unsigned int count, gen;
+};
+
+__device__ __forceinline__ bool grid_barrier(RouteSync* gs, unsigned nblocks, const WaitCfg& wc) {
+  __shared__ int ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned g0 = *(volatile unsigned*)&gs->gen;  // read before arriving
+    __threadfence();
+    const unsigned prev = atomicAdd(&gs->count, 1u);
+    if (prev == nblocks - 1) {
+      gs->count = 0;  // every CTA has arrived: reset for the next launch, then release
+      __threadfence();
+      atomicAdd(&gs->gen, 1u);
+      ok = 1;
+    } else {
+      ok = 1;
+      const unsigned long long t0 = globaltimer_ns();
+      for (uint32_t it = 0; *(volatile unsigned*)&gs->gen == g0; ++it) {
+        __nanosleep(32);
+        if ((it & 255u) == 255u && globaltimer_ns() - t0 > wc.timeout_ns) {
+          set_err(wc.err, kErrPipeline);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__global__ void __launch_bounds__(kRouteThreads) k_route_fused(
+    int64_t n, int k, int E, int64_t tpc, int world, int rank, const int64_t* __restrict__ idx,
+    const uint8_t* __restrict__ valid, const int32_t* __restrict__ owners,
+    const int32_t* __restrict__ nrep, int64_t* __restrict__ rr, int64_t* __restrict__ route_counts,
+    int32_t* __restrict__ chunk_hist, int32_t* __restrict__ ent_dest,
+    int32_t* __restrict__ ent_grp, int32_t* __restrict__ my_counts, PeerPtrs peers, uint32_t* seq,
+    RouteSync* gs, WaitCfg wc) {
+  __shared__ int hist[kMaxExperts];
+  __shared__ int base[kMaxExperts];   // entries of expert e before this CTA's range, then running
+  __shared__ int tot[kMaxExperts];
+  __shared__ int rr_mod[kMaxExperts];
+  __shared__ int wcnt[kRouteWarps][kMaxExperts];
+  __shared__ int wbase[kRouteWarps][kMaxExperts];
+  __shared__ int cnt[kMaxWorld * kMaxExperts];
+  __shared__ int any_rep;
+  const int wp = warp_id(), lane = lane_id();
+  const int b = blockIdx.x;
+  const int64_t t_beg = min((int64_t)b * tpc, n), t_end = min(t_beg + tpc, n);
+
+  // ---- phase 1: round-robin state (read before anyone updates it), local histogram
+  if (threadIdx.x == 0) any_rep = 0;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    hist[e] = 0;
+    base[e] = 0;
+    tot[e] = 0;
+    rr_mod[e] = (int)(rr[e] % nrep[e]);
+  }
+  __syncthreads();
+  for (int64_t f = t_beg * k + threadIdx.x; f < t_end * k; f += blockDim.x) {
+    const int e = entry_expert(idx, valid, f, k, n, E, wc.err);
+    if (e >= 0) atomicAdd(&hist[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_hist[(int64_t)b * E + e] = hist[e];
+  grid_barrier(gs, gridDim.x, wc);
+
+  // ---- phase 2: prefix of the earlier CTAs' counts and the totals
+  {
+    const int parts = blockDim.x / E > 0 ? blockDim.x / E : 1;
+    for (int i = threadIdx.x; i < parts * E; i += blockDim.x) {
+      const int e = i % E, part = i / E;
+      int bsum = 0, tsum = 0;
+      for (int c = part; c < (int)gridDim.x; c += parts) {
+        const int v = __ldcg(chunk_hist + (int64_t)c * E + e);
+        tsum += v;
+        if (c < b) bsum += v;
+      }
+      if (bsum) atomicAdd(&base[e], bsum);
+      if (tsum) atomicAdd(&tot[e], tsum);
+    }
+  }
+  __syncthreads();
+
+  if (b == 0) {
+    // finalize (k_route_finalize's work): counts per (dest, expert), rr, stats, publish
+    const uint32_t step = *seq + 1u;
+    for (int i = threadIdx.x; i < world * E; i += blockDim.x) cnt[i] = 0;
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+      if (nrep[e] > 1) any_rep = 1;
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      const int c = tot[e];
+      const int nr = nrep[e];
+      const int rr0 = rr_mod[e];
+      for (int j = 0; j < nr; ++j) {
+        const int d = owners[e * kMaxWorld + j];
+        const int w0 = ((j - rr0) % nr + nr) % nr;
+        cnt[d * E + e] = c > w0 ? (c - w0 - 1) / nr + 1 : 0;
+      }
+      if (any_rep) rr[e] += c;
+      if (route_counts) route_counts[e] += c;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < world * E; i += blockDim.x) my_counts[i] = cnt[i];
+    for (int d = 0; d < world; ++d) {
+      int32_t* dst = peers.cnt_in[d] + (int64_t)rank * world * E;
+      for (int i = threadIdx.x; i < world * E; i += blockDim.x) dst[i] = cnt[i];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, step);
+    __syncthreads();
+    if (threadIdx.x == 0) *seq = step;
+  }
+
+  // ---- ranking, 256 tokens per round (8 warps x 32 tokens)
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int64_t r0 = t_beg; r0 < t_end; r0 += kRouteChunkTokens) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+      for (int w = 0; w < kRouteWarps; ++w) wcnt[w][e] = 0;
+    __syncthreads();
+    const int64_t t0 = r0 + wp * 32;
+    const int64_t f0 = t0 * k;
+    const int64_t f_end = min(r0 + kRouteChunkTokens, t_end) * k;
+    for (int r = 0; r < k; ++r) {
+      const int64_t f = f0 + r * 32 + lane;
+      const int e = f < f_end ? entry_expert(idx, valid, f, k, n, E, nullptr) : -1;
+      if (e >= 0) atomicAdd(&wcnt[wp][e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int run = 0;
+      for (int w = 0; w < kRouteWarps; ++w) {
+        wbase[w][e] = run;
+        run += wcnt[w][e];
+        wcnt[w][e] = 0;  // reused as the running count of the pass below
+      }
+      hist[e] = run;  // this round's total, added to base after the pass
+    }
+    __syncthreads();
+    for (int r = 0; r < k; ++r) {
+      const int64_t f = f0 + r * 32 + lane;
+      const int e = f < f_end ? entry_expert(idx, valid, f, k, n, E, nullptr) : -1;
+      const unsigned peers_mask = __match_any_sync(0xffffffffu, e);
+      const int rank_in_round = __popc(peers_mask & lt_mask);
+      int dest = -1, grp = 0;
+      if (e >= 0) {
+        const int within = base[e] + wbase[wp][e] + wcnt[wp][e] + rank_in_round;
+        const int nr = nrep[e];
+        const int slot = (rr_mod[e] + within) % nr;
+        dest = owners[e * kMaxWorld + slot];
+        grp = within / nr;
+      }
+      __syncwarp();
+      if (e >= 0 && rank_in_round == 0) wcnt[wp][e] += __popc(peers_mask);
+      __syncwarp();
+      if (f < f_end) {
+        ent_dest[f] = dest;
+        ent_grp[f] = grp;
+      }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] += hist[e];
+    __syncthreads();
+  }
+}
+
 __global__ void k_dest_to_i64(int64_t m, const int32_t* __restrict__ d, int64_t* __restrict__ out) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < m) out[i] = d[i];
@@ -262,16 +445,17 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   const int64_t* topk_idx, const uint8_t* valid, const int32_t* owners_l,
                   const int32_t* nrep_l, int64_t* rr_l, int64_t* route_counts_l,
                   int32_t* chunk_hist, int32_t* ent_dest, int32_t* ent_grp, int32_t* my_counts,
-                  const PeerPtrs& peers, uint32_t* seq, WaitCfg wc, cudaStream_t st) {
-  const int nchunks = (int)((n + kRouteChunkTokens - 1) / kRouteChunkTokens);
-  if (nchunks > 0) {
-    k_route_hist<<<nchunks, kRouteThreads, 0, st>>>(n, topk, experts, topk_idx, valid, chunk_hist,
-                                                    wc.err);
-    k_route_rank<<<nchunks, kRouteThreads, 0, st>>>(n, topk, experts, topk_idx, valid, owners_l,
-                                                    nrep_l, rr_l, chunk_hist, ent_dest, ent_grp);
-  }
-  k_route_finalize<<<1, 256, 0, st>>>(nchunks, experts, world, rank, owners_l, nrep_l, rr_l,
-                                      route_counts_l, chunk_hist, my_counts, peers, seq, 1);
+                  const PeerPtrs& peers, uint32_t* seq, unsigned int* sync, int num_sms,
+                  WaitCfg wc, cudaStream_t st) {
+  // one CTA per 256-token round, at most one per SM (all resident for the grid barrier)
+  const int64_t rounds = (n + kRouteChunkTokens - 1) / kRouteChunkTokens;
+  int64_t grid = rounds < num_sms ? rounds : num_sms;
+  if (grid < 1) grid = 1;
+  const int64_t tpc = (rounds + grid - 1) / grid * kRouteChunkTokens;
+  k_route_fused<<<(unsigned)grid, kRouteThreads, 0, st>>>(
+      n, topk, experts, tpc, world, rank, topk_idx, valid, owners_l, nrep_l, rr_l, route_counts_l,
+      chunk_hist, ent_dest, ent_grp, my_counts, peers, seq, reinterpret_cast<RouteSync*>(sync),
+      wc);
 }
 
 void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids, const int32_t* owners_l,

@@ -225,9 +225,15 @@ __global__ void __launch_bounds__(128) k_router_simt(
 
 void launch_router(int dtype, const void* x, const void* router_w, const float* bias, int64_t n,
                    int hidden, int experts, int topk, int64_t* idx_out, void* gate_out,
-                   float* logits_out, cudaStream_t st) {
+                   float* logits_out, int num_sms, int* err, cudaStream_t st) {
+  (void)num_sms;
+  (void)err;
   if (n <= 0) return;
-  if (dtype == kBF16 && hidden % 64 == 0 && experts % 8 == 0 && experts <= 64) {
+  // the tensor-core kernel reads x and the router rows in 16-byte pieces; the
+  // CUDA-core kernel takes any layout
+  const bool aligned16 = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(router_w)) &
+                          15u) == 0;
+  if (dtype == kBF16 && hidden % 64 == 0 && experts % 8 == 0 && experts <= 64 && aligned16) {
     const unsigned grid = (unsigned)((n + 15) / 16);
     auto xb = static_cast<const bf16*>(x);
     auto wb = static_cast<const bf16*>(router_w);

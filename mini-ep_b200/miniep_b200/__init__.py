@@ -7,10 +7,10 @@ formats; the layer step runs in libminiep_b200.so (C ABI in
 include/miniep_b200.h).
 """
 from .ep import (Comm, EPMoEBackend, EPStats, GraphedMoEBlock, LocalMoEBackend,  # noqa: F401
-                 Placement, router_topk)
+                 Placement, StreamedMoEBlock, router_topk)
 from .balancer import layer_imbalance, plan_balanced, straggler_overhead  # noqa: F401
 from ._lib import MEPError  # noqa: F401
 
 __all__ = ["Comm", "EPMoEBackend", "EPStats", "GraphedMoEBlock", "LocalMoEBackend", "Placement",
-           "router_topk",
+           "StreamedMoEBlock", "router_topk",
            "plan_balanced", "straggler_overhead", "layer_imbalance", "MEPError"]

@@ -425,6 +425,65 @@ class GraphedMoEBlock:
         return self.h_out
 
 
+class StreamedMoEBlock:
+    """``GraphedMoEBlock`` for token batches that live in (pinned) host memory.
+
+    The batch is cut into ``chunks`` pieces, each with its own captured layer
+    step. Piece i's host-to-device copy runs on one stream, its layer step on
+    the caller's stream and its device-to-host copy on a third, so the copies
+    of one piece overlap the steps of the others (and, across calls, the next
+    batch's first copies overlap this batch's last step). Each piece is one
+    layer call of the reference's contract: routing, replica round-robin and
+    stats advance per piece exactly as for consecutive eager calls, and every
+    output row is bit-identical to the unchunked step's.
+
+    Every rank must use the same ``chunks`` and call in lockstep.
+    """
+
+    def __init__(self, backend: "EPMoEBackend", n_tokens: int, router_w,
+                 residual_multiplier: float, bias=None, chunks: int = 4):
+        if n_tokens < 1 or chunks < 1:
+            raise ValueError("StreamedMoEBlock: n_tokens and chunks must be positive")
+        chunks = min(chunks, n_tokens)
+        base, extra = divmod(n_tokens, chunks)
+        self.sizes = [base + (1 if i < extra else 0) for i in range(chunks)]
+        self.n = n_tokens
+        self.blocks = [GraphedMoEBlock(backend, m, router_w, residual_multiplier, bias=bias)
+                       for m in self.sizes]
+        self.copy_in = torch.cuda.Stream()
+        self.copy_out = torch.cuda.Stream()
+        ev = lambda: [torch.cuda.Event() for _ in self.sizes]  # noqa: E731
+        self.loaded, self.stepped, self.inputs_free, self.output_free = ev(), ev(), ev(), ev()
+
+    def __call__(self, x_host, h_host, out_host):
+        """Enqueue ``out_host = h_host + moe(x_host) * rm`` on the current
+        stream. The host tensors must be pinned for the copies to overlap;
+        ``out_host`` is complete once the current stream reaches this point."""
+        if x_host.shape[0] != self.n or h_host.shape[0] != self.n or out_host.shape[0] != self.n:
+            raise ValueError(f"StreamedMoEBlock: expected {self.n} tokens")
+        cur = torch.cuda.current_stream()
+        off = 0
+        for i, (blk, m) in enumerate(zip(self.blocks, self.sizes)):
+            rows = slice(off, off + m)
+            off += m
+            with torch.cuda.stream(self.copy_in):
+                self.copy_in.wait_event(self.inputs_free[i])  # last call's step i read blk.x / blk.h
+                blk.x.copy_(x_host[rows], non_blocking=True)
+                blk.h.copy_(h_host[rows], non_blocking=True)
+                self.loaded[i].record(self.copy_in)
+            cur.wait_event(self.loaded[i])
+            cur.wait_event(self.output_free[i])  # last call's copy-out of blk.h_out is done
+            blk.graph.replay()
+            self.inputs_free[i].record(cur)
+            self.stepped[i].record(cur)
+            with torch.cuda.stream(self.copy_out):
+                self.copy_out.wait_event(self.stepped[i])
+                out_host[rows].copy_(blk.h_out, non_blocking=True)
+                self.output_free[i].record(self.copy_out)
+        cur.wait_stream(self.copy_out)
+        return out_host
+
+
 def router_topk(comm: Comm, x_flat, router_w, bias=None, return_logits: bool = False):
     """Router of ``Block.forward`` (miniep/modeling.py:193-195) on the device:
     (topk_idx int64, topk_gate model dtype[, logits fp32])."""

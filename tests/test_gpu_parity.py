@@ -62,7 +62,7 @@ def test_router_fp32_config1(golden):
                           rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("shape,n", [("a", 4096), ("b", 1024)])
+@pytest.mark.parametrize("shape,n", [("a", 4096), ("a", 1), ("a", 1000), ("b", 1024), ("b", 33)])
 def test_router_bf16_skewed(shape, n):
     sh = synth.SHAPES[shape]
     lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=1, dtype=torch.bfloat16)
@@ -76,7 +76,8 @@ def test_router_bf16_skewed(shape, n):
     ulp = ref_logits.float().abs().clamp_min(2.0 ** -20) * 2.0 ** -7
     assert torch.all((logits - ref_logits.float()).abs() <= ulp)
     same_row = (logits == ref_logits.float()).all(dim=1)
-    assert same_row.float().mean() > 0.9
+    if n >= 64:
+        assert same_row.float().mean() > 0.9
     # selection rule is exact on the kernel's own logits (lower index first on ties)
     assert torch.equal(idx, O.topk_lowest_index(logits, sh["topk"]))
     # against the reference: bit-exact wherever the logits agree and hold no tie
@@ -88,6 +89,25 @@ def test_router_bf16_skewed(shape, n):
     # per-expert histogram of the kernel's routing == the reference's on tie-free rows
     assert torch.equal(torch.bincount(idx[ok].reshape(-1), minlength=sh["experts"]),
                        torch.bincount(ref_idx[ok].reshape(-1), minlength=sh["experts"]))
+
+
+def test_router_bf16_rows_not_16_byte_aligned():
+    """x starting 4 bytes past an allocation takes the CUDA-core kernel; its
+    logits and selection obey the same contract as the staged kernel's."""
+    sh = synth.SHAPES["a"]
+    n, H = 200, sh["hidden"]
+    lb = synth.make_layer(H, sh["experts"], sh["inter"], n, seed=3, dtype=torch.bfloat16)
+    buf = torch.empty(n * H + 2, dtype=torch.bfloat16, device="cuda")
+    x = buf[2:].view(n, H)
+    x.copy_(lb.x)
+    assert x.data_ptr() % 16 == 4
+    comm = world1_comm(sh["experts"], sh["topk"], H, sh["inter"], n, torch.bfloat16)
+    idx, gate, logits = router_topk(comm, x, lb.router.cuda(), return_logits=True)
+    idx, logits = idx.cpu(), logits.cpu()
+    _, _, ref_logits = O.router_topk(lb.x, lb.router, sh["topk"])
+    ulp = ref_logits.float().abs().clamp_min(2.0 ** -20) * 2.0 ** -7
+    assert torch.all((logits - ref_logits.float()).abs() <= ulp)
+    assert torch.equal(idx, O.topk_lowest_index(logits, sh["topk"]))
 
 
 # ---------------------------------------------------------------- dest ranks
@@ -250,10 +270,12 @@ def test_empty_masked_and_single_hot_expert():
     be.comm.check()
 
 
-def test_full_size_workload_properties():
-    """BASELINE shape (a) at 16K tokens: counts exact, sampled rows vs the checker."""
+@pytest.mark.parametrize("n", [16384, 65536])
+def test_full_size_workload_properties(n):
+    """BASELINE shape (a) at 16K and 64K tokens (64K: more 256-token routing
+    rounds than SMs, so routing CTAs take several rounds each): counts exact,
+    sampled rows vs the checker."""
     sh = synth.SHAPES["a"]
-    n = 16384
     lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=0, dtype=torch.bfloat16)
     bias = synth.zipf_router_bias(1, sh["experts"])[0]
     be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
@@ -331,4 +353,33 @@ def test_graphed_block_replays_match_eager_calls():
         got = blk(x, h).clone()
         want, _, _ = be.moe_block(h, x, router, synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
         assert torch.equal(got, want)
+    be.comm.check()
+
+
+def test_streamed_block_from_host_matches_unchunked_step():
+    """Host batches through StreamedMoEBlock (chunked copies overlapping the
+    steps, ragged last chunk) give the unchunked step's rows bit for bit, on
+    two consecutive calls that reuse the same pinned buffers."""
+    from miniep_b200 import StreamedMoEBlock
+    sh = synth.SHAPES["a"]
+    n = 1000
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], 2 * n, seed=12,
+                          dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0].cuda()
+    hs = synth.make_tokens(2 * n, sh["hidden"], seed=13, dtype=torch.bfloat16)
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
+    router = lb.router.cuda()
+    blk = StreamedMoEBlock(be, n, router, synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias, chunks=3)
+    assert blk.sizes == [334, 333, 333]
+    x_host = torch.empty(n, sh["hidden"], dtype=torch.bfloat16).pin_memory()
+    h_host = torch.empty_like(x_host).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    for part in (1, 0):
+        x_host.copy_(lb.x[part * n:(part + 1) * n])
+        h_host.copy_(hs[part * n:(part + 1) * n])
+        blk(x_host, h_host, out_host)
+        torch.cuda.synchronize()
+        want, _, _ = be.moe_block(h_host.cuda(), x_host.cuda(), router,
+                                  synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
+        assert torch.equal(out_host, want.cpu())
     be.comm.check()
