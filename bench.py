@@ -40,8 +40,8 @@ METRIC = "MoE layer tokens/s"
 UNIT = "tokens/s"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_BF16_TFLOPS = 1590.0
-# router, hist, rank, finalize, layout, dispatch, wait, gemm1, gemm2, combine (+ fan-out when N > 1)
-KERNELS_PER_STEP = 10
+# router, routing (+ layout), dispatch, gemm1, gemm2, combine (+ data wait and fan-out when N > 1)
+KERNELS_PER_STEP = 6
 
 
 def parse():
@@ -405,7 +405,7 @@ def main_b200(a):
                                     / (ms_step / 1e3) / 1e12) / peak,
             "recv_rows_total": total_rows,
             "wall_s_timed_region": wall,
-            "gpu_launches": (KERNELS_PER_STEP + (world > 1)) * a.steps,
+            "gpu_launches": (KERNELS_PER_STEP + 2 * (world > 1)) * a.steps,
             "clocks": clk,
         }
         if e2e:

@@ -364,8 +364,10 @@ int mep_route(mep_ctx* c, int layer, const int64_t* topk_idx, const uint8_t* val
   launch_route(n, c->k, c->E, c->world, c->rank, topk_idx, valid, owners_of(c, layer),
                nrep_of(c, layer), c->rr + (int64_t)layer * c->E,
                c->route_counts + (int64_t)layer * c->E, c->chunk_hist, c->ent_dest, c->ent_grp,
-               c->my_counts, c->peers, c->seq, c->done_ctr + 2, c->num_sms, wait_cfg(c),
-               as_stream(stream));
+               c->my_counts, c->peers, c->seq, c->done_ctr + 2, c->num_sms,
+               reinterpret_cast<const int32_t*>(c->sym + c->off_cnt),
+               reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->recv_per_layer + layer,
+               c->cap_rows, c->layout, wait_cfg(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   c->stage = 1;
   return MEP_OK;
@@ -377,24 +379,20 @@ int mep_dispatch(mep_ctx* c, const void* x, const int64_t* topk_idx, int64_t n, 
   if (n != c->cur_n) return fail(c, MEP_ERR_INVALID, "n differs from the routed step");
   if (n > 0 && (!x || !topk_idx)) return fail(c, MEP_ERR_INVALID, "NULL argument");
   if (int rc = use_device(c)) return rc;
-  const int layer = c->cur_layer;
-  launch_layout(c->world, c->rank, c->E, owners_of(c, layer), nrep_of(c, layer),
-                reinterpret_cast<const int32_t*>(c->sym + c->off_cnt),
-                reinterpret_cast<const uint32_t*>(c->sym + c->off_flags),
-                c->recv_per_layer + layer, c->cap_rows, c->layout, c->seq, wait_cfg(c),
-                as_stream(stream));
+  // the receive layout was computed by mep_route's kernel
   launch_dispatch(c->dtype, n, c->k, c->H, c->world, c->rank, c->max_tokens,
                   x, topk_idx, c->ent_dest,
                   c->ent_grp, c->layout, c->peers, c->done_ctr, c->seq, c->num_sms,
                   as_stream(stream));
   // the stage ends when every rank's rows for this rank have landed and sit in
-  // their expert-segment rows
-  launch_wait_flags(reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->world, c->world,
-                    c->seq, 0u, kErrWaitData, wait_cfg(c), as_stream(stream));
-  if (c->world > 1)
+  // their expert-segment rows (one rank: stream order already says so)
+  if (c->world > 1) {
+    launch_wait_flags(reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->world,
+                      c->world, c->seq, 0u, kErrWaitData, wait_cfg(c), as_stream(stream));
     launch_fanout(c->dtype, c->H, c->k, c->rank, c->max_tokens, c->layout,
                   reinterpret_cast<const int32_t*>(c->sym + c->off_meta), c->sym + c->off_land,
                   c->recv_x, c->num_sms, as_stream(stream));
+  }
   MEP_CK(c, cudaGetLastError());
   c->stage = 2;
   return MEP_OK;

@@ -69,17 +69,16 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,
                   int64_t* route_counts_l, int32_t* chunk_hist, int32_t* ent_dest,
                   int32_t* ent_grp, int32_t* my_counts, const PeerPtrs& peers,
-                  uint32_t* seq, unsigned int* sync, int num_sms, WaitCfg wc, cudaStream_t st);
+                  uint32_t* seq, unsigned int* sync, int num_sms,
+                  const int32_t* cnt_in_local, const uint32_t* flags_local,
+                  int64_t* recv_per_layer_l, int64_t cap_rows, Layout* layout, WaitCfg wc,
+                  cudaStream_t st);
 
 void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids,
                       const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,
                       int32_t* chunk_hist, int32_t* ent_dest, int32_t* ent_grp,
                       int32_t* my_counts, int64_t* dest_out, WaitCfg wc, cudaStream_t st);
 
-void launch_layout(int world, int rank, int experts, const int32_t* owners_l,
-                   const int32_t* nrep_l, const int32_t* cnt_in_local,
-                   const uint32_t* flags_local, int64_t* recv_per_layer_l, int64_t cap_rows,
-                   Layout* layout, const uint32_t* seq, WaitCfg wc, cudaStream_t st);
 
 // ---------------------------------------------------------------- movement
 void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int rank,

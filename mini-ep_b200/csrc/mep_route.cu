@@ -180,6 +180,74 @@ __global__ void __launch_bounds__(256) k_route_finalize(
   if (threadIdx.x == 0) *seq = step;
 }
 
+// Receive layout + send offsets from the exchanged counts C[s][d][e], by one
+// CTA, once every rank's counts for step `step` have arrived (bounded wait).
+__device__ void layout_block(int world, int rank, int E, const int32_t* __restrict__ owners,
+                             const int32_t* __restrict__ nrep, const int32_t* cnt_in,
+                             const uint32_t* flags, int64_t* __restrict__ recv_per_layer,
+                             int64_t cap_rows, Layout* __restrict__ lay, uint32_t step,
+                             const WaitCfg& wc) {
+  __shared__ int R[kMaxWorld][kMaxExperts];       // rows per (dest, expert)
+  __shared__ int before[kMaxWorld][kMaxExperts];  // rows from sources < rank
+  __shared__ int seg[kMaxWorld][kMaxExperts];
+  __shared__ unsigned char res[kMaxWorld][kMaxExperts];
+  __shared__ int overflow[kMaxWorld];
+  if (threadIdx.x < world) wait_flag(flags + threadIdx.x, step, kErrWaitCounts, wc);
+  __syncthreads();
+  for (int i = threadIdx.x; i < world * E; i += blockDim.x) {
+    const int d = i / E, e = i % E;
+    int tot = 0, bef = 0;
+    for (int s = 0; s < world; ++s) {
+      const int c = __ldcv(cnt_in + ((int64_t)s * world + d) * E + e);
+      tot += c;
+      if (s < rank) bef += c;
+    }
+    R[d][e] = tot;
+    before[d][e] = bef;
+    unsigned char r = 0;
+    for (int j = 0; j < nrep[e]; ++j) r |= owners[e * kMaxWorld + j] == d;
+    res[d][e] = r;
+    if (tot > 0 && !r) set_err(wc.err, kErrNotResident);
+  }
+  __syncthreads();
+  if (threadIdx.x < world) {
+    const int d = threadIdx.x;
+    int64_t b = 0;
+    for (int e = 0; e < E; ++e) {
+      seg[d][e] = (int)b;
+      if (res[d][e]) b += (R[d][e] + kRowAlign - 1) / kRowAlign * kRowAlign;
+    }
+    overflow[d] = b > cap_rows;
+    if (b > cap_rows) set_err(wc.err, kErrCapacity);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < world * E; i += blockDim.x) {
+    const int d = i / E, e = i % E;
+    lay->dst_off[d * kMaxExperts + e] = overflow[d] ? -1 : seg[d][e] + before[d][e];
+  }
+  if (threadIdx.x == 0) {
+    int j = 0, tiles = 0, rows = 0, end = 0;
+    for (int e = 0; e < E; ++e) {
+      if (!res[rank][e]) continue;
+      lay->local_expert[j] = e;
+      lay->seg_base[j] = seg[rank][e];
+      lay->seg_rows[j] = R[rank][e];
+      lay->tile_prefix[j] = tiles;
+      const int t = (R[rank][e] + kRowAlign - 1) / kRowAlign;
+      tiles += t;
+      rows += R[rank][e];
+      end = seg[rank][e] + t * kRowAlign;
+      ++j;
+    }
+    lay->tile_prefix[j] = tiles;
+    lay->n_local = j;
+    lay->total_mtiles = overflow[rank] ? 0 : tiles;
+    lay->total_rows = end;
+    lay->recv_rows = rows;
+    if (recv_per_layer) recv_per_layer[0] += rows;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // The three routing passes above as ONE launch, for the layer step.
 //
@@ -231,7 +299,8 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     const int32_t* __restrict__ nrep, int64_t* __restrict__ rr, int64_t* __restrict__ route_counts,
     int32_t* __restrict__ chunk_hist, int32_t* __restrict__ ent_dest,
     int32_t* __restrict__ ent_grp, int32_t* __restrict__ my_counts, PeerPtrs peers, uint32_t* seq,
-    RouteSync* gs, WaitCfg wc) {
+    RouteSync* gs, const int32_t* cnt_in, const uint32_t* flags, int64_t* recv_per_layer,
+    int64_t cap_rows, Layout* lay, WaitCfg wc) {
   __shared__ int hist[kMaxExperts];
   __shared__ int base[kMaxExperts];   // entries of expert e before this CTA's range, then running
   __shared__ int tot[kMaxExperts];
@@ -309,6 +378,10 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, step);
     __syncthreads();
     if (threadIdx.x == 0) *seq = step;
+    // the receive layout, once every rank's counts are in (the other CTAs rank meanwhile)
+    layout_block(world, rank, E, owners, nrep, cnt_in, flags, recv_per_layer, cap_rows, lay, step,
+                 wc);
+    __syncthreads();
   }
 
   // ---- ranking, 256 tokens per round (8 warps x 32 tokens)
@@ -368,77 +441,6 @@ __global__ void k_dest_to_i64(int64_t m, const int32_t* __restrict__ d, int64_t*
   if (i < m) out[i] = d[i];
 }
 
-// Receive layout + send offsets from the exchanged counts C[s][d][e].
-__global__ void __launch_bounds__(256) k_layout(int world, int rank, int E,
-                                                const int32_t* __restrict__ owners,
-                                                const int32_t* __restrict__ nrep,
-                                                const int32_t* __restrict__ cnt_in,
-                                                const uint32_t* __restrict__ flags,
-                                                int64_t* __restrict__ recv_per_layer,
-                                                int64_t cap_rows, Layout* __restrict__ lay,
-                                                const uint32_t* seq, WaitCfg wc) {
-  const uint32_t step = *seq;
-  __shared__ int R[kMaxWorld][kMaxExperts];       // rows per (dest, expert)
-  __shared__ int before[kMaxWorld][kMaxExperts];  // rows from sources < rank
-  __shared__ int seg[kMaxWorld][kMaxExperts];
-  __shared__ unsigned char res[kMaxWorld][kMaxExperts];
-  __shared__ int overflow[kMaxWorld];
-  if (threadIdx.x < world) wait_flag(flags + threadIdx.x, step, kErrWaitCounts, wc);
-  __syncthreads();
-  for (int i = threadIdx.x; i < world * E; i += blockDim.x) {
-    const int d = i / E, e = i % E;
-    int tot = 0, bef = 0;
-    for (int s = 0; s < world; ++s) {
-      const int c = cnt_in[((int64_t)s * world + d) * E + e];
-      tot += c;
-      if (s < rank) bef += c;
-    }
-    R[d][e] = tot;
-    before[d][e] = bef;
-    unsigned char r = 0;
-    for (int j = 0; j < nrep[e]; ++j) r |= owners[e * kMaxWorld + j] == d;
-    res[d][e] = r;
-    if (tot > 0 && !r) set_err(wc.err, kErrNotResident);
-  }
-  __syncthreads();
-  if (threadIdx.x < world) {
-    const int d = threadIdx.x;
-    int64_t b = 0;
-    for (int e = 0; e < E; ++e) {
-      seg[d][e] = (int)b;
-      if (res[d][e]) b += (R[d][e] + kRowAlign - 1) / kRowAlign * kRowAlign;
-    }
-    overflow[d] = b > cap_rows;
-    if (b > cap_rows) set_err(wc.err, kErrCapacity);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < world * E; i += blockDim.x) {
-    const int d = i / E, e = i % E;
-    lay->dst_off[d * kMaxExperts + e] = overflow[d] ? -1 : seg[d][e] + before[d][e];
-  }
-  if (threadIdx.x == 0) {
-    int j = 0, tiles = 0, rows = 0, end = 0;
-    for (int e = 0; e < E; ++e) {
-      if (!res[rank][e]) continue;
-      lay->local_expert[j] = e;
-      lay->seg_base[j] = seg[rank][e];
-      lay->seg_rows[j] = R[rank][e];
-      lay->tile_prefix[j] = tiles;
-      const int t = (R[rank][e] + kRowAlign - 1) / kRowAlign;
-      tiles += t;
-      rows += R[rank][e];
-      end = seg[rank][e] + t * kRowAlign;
-      ++j;
-    }
-    lay->tile_prefix[j] = tiles;
-    lay->n_local = j;
-    lay->total_mtiles = overflow[rank] ? 0 : tiles;
-    lay->total_rows = end;
-    lay->recv_rows = rows;
-    if (recv_per_layer) recv_per_layer[0] += rows;
-  }
-}
-
 }  // namespace
 
 void launch_route(int64_t n, int topk, int experts, int world, int rank,
@@ -446,7 +448,9 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   const int32_t* nrep_l, int64_t* rr_l, int64_t* route_counts_l,
                   int32_t* chunk_hist, int32_t* ent_dest, int32_t* ent_grp, int32_t* my_counts,
                   const PeerPtrs& peers, uint32_t* seq, unsigned int* sync, int num_sms,
-                  WaitCfg wc, cudaStream_t st) {
+                  const int32_t* cnt_in_local, const uint32_t* flags_local,
+                  int64_t* recv_per_layer_l, int64_t cap_rows, Layout* layout, WaitCfg wc,
+                  cudaStream_t st) {
   // one CTA per 256-token round, at most one per SM (all resident for the grid barrier)
   const int64_t rounds = (n + kRouteChunkTokens - 1) / kRouteChunkTokens;
   int64_t grid = rounds < num_sms ? rounds : num_sms;
@@ -455,7 +459,7 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
   k_route_fused<<<(unsigned)grid, kRouteThreads, 0, st>>>(
       n, topk, experts, tpc, world, rank, topk_idx, valid, owners_l, nrep_l, rr_l, route_counts_l,
       chunk_hist, ent_dest, ent_grp, my_counts, peers, seq, reinterpret_cast<RouteSync*>(sync),
-      wc);
+      cnt_in_local, flags_local, recv_per_layer_l, cap_rows, layout, wc);
 }
 
 void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids, const int32_t* owners_l,
@@ -475,12 +479,5 @@ void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids, const i
                                       nullptr, chunk_hist, my_counts, none, nullptr, 0);
 }
 
-void launch_layout(int world, int rank, int experts, const int32_t* owners_l,
-                   const int32_t* nrep_l, const int32_t* cnt_in_local, const uint32_t* flags_local,
-                   int64_t* recv_per_layer_l, int64_t cap_rows, Layout* layout, const uint32_t* seq,
-                   WaitCfg wc, cudaStream_t st) {
-  k_layout<<<1, 256, 0, st>>>(world, rank, experts, owners_l, nrep_l, cnt_in_local, flags_local,
-                              recv_per_layer_l, cap_rows, layout, seq, wc);
-}
 
 }  // namespace mep
