@@ -211,7 +211,7 @@ def run_reference(a):
 def main_b200(a):
     import torch.distributed as dist
     from miniep_b200 import (Comm, EPMoEBackend, GraphedMoEBlock, Placement, StreamedMoEBlock, _lib,
-                             plan_balanced, synth)
+                             plan_balanced, straggler_overhead, synth)
     from miniep_b200.ep import router_topk
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -239,6 +239,7 @@ def main_b200(a):
     if a.force_simt:
         comm.set_option("force_simt", 1)
     placement = Placement.naive(1, E, world)
+    counts = None
     if world > 1 and a.plan == "balanced":
         comm.install(placement)
         idx, _ = router_topk(comm, x, lt.router, bias)
@@ -369,7 +370,13 @@ def main_b200(a):
         comm.check()
     clk = clocks.stop()
 
+    # per-rank received rows and expert-stage time: the straggler figures
+    per_rank = torch.tensor([[float(recv_rows), sum(ffn_ms) / n_eager]], device=dev,
+                            dtype=torch.float64)
     if world > 1:
+        parts = [torch.zeros_like(per_rank) for _ in range(world)]
+        dist.all_gather(parts, per_rank)
+        per_rank = torch.cat(parts)
         dist.all_reduce(rows_t)
     total_rows = rows_t.item()
     cpu = None
@@ -408,6 +415,19 @@ def main_b200(a):
             "gpu_launches": (KERNELS_PER_STEP + 2 * (world > 1)) * a.steps,
             "clocks": clk,
         }
+        if world > 1:
+            loads = per_rank[:, 0].cpu().view(world, 1)
+            t_ffn = per_rank[:, 1].cpu()
+            strag = {"formula": "sum_l max_r recv / sum_l mean_r recv - 1 (1 layer)",
+                     "plan": a.plan,
+                     "load_pct": 100.0 * straggler_overhead(loads),
+                     "ffn_time_pct": 100.0 * float(t_ffn.max() / t_ffn.mean() - 1.0),
+                     "recv_rows_per_rank": loads.view(-1).tolist()}
+            if counts is not None:  # what the naive placement would have given
+                per = E // world
+                naive = counts.cpu().view(world, per).sum(dim=1).view(world, 1)
+                strag["naive_load_pct"] = 100.0 * straggler_overhead(naive)
+            line["straggler"] = strag
         if e2e:
             line["e2e"] = e2e
         if cpu:

@@ -118,7 +118,8 @@ int mep_router_topk(mep_ctx* ctx, const void* x, const void* router_w, const flo
  * Updates route_counts[layer] and recv_tokens_per_layer[layer].
  *   replaces: EPMoEBackend.__call__ (miniep/ep.py:210-249), which is also
  *             LocalMoEBackend.__call__ (miniep/modeling.py:138-145) at world 1
- * x: (n, H); topk_idx: (n, k) int64; topk_gate: (n, k) model dtype;
+ * x: (n, H), rows contiguous, starting on a 16-byte boundary; topk_idx: (n, k)
+ * int64; topk_gate: (n, k) model dtype;
  * valid: (n,) uint8 or NULL (all valid); w_in: (n_local, 2I, H) and
  * w_out: (n_local, H, I) for this rank's experts of `layer` in increasing
  * expert order; out: (n, H).

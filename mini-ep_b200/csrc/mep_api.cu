@@ -378,6 +378,8 @@ int mep_dispatch(mep_ctx* c, const void* x, const int64_t* topk_idx, int64_t n, 
   if (c->stage != 1) return fail(c, MEP_ERR_STATE, "mep_dispatch must follow mep_route");
   if (n != c->cur_n) return fail(c, MEP_ERR_INVALID, "n differs from the routed step");
   if (n > 0 && (!x || !topk_idx)) return fail(c, MEP_ERR_INVALID, "NULL argument");
+  if (n > 0 && (reinterpret_cast<uintptr_t>(x) & 15u) != 0)  // rows are read in 16-byte pieces
+    return fail(c, MEP_ERR_INVALID, "x must start on a 16-byte boundary");
   if (int rc = use_device(c)) return rc;
   // the receive layout was computed by mep_route's kernel
   launch_dispatch(c->dtype, n, c->k, c->H, c->world, c->rank, c->max_tokens,

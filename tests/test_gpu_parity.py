@@ -91,6 +91,23 @@ def test_router_bf16_skewed(shape, n):
                        torch.bincount(ref_idx[ok].reshape(-1), minlength=sh["experts"]))
 
 
+def test_dispatch_rejects_rows_not_16_byte_aligned():
+    sh = synth.SHAPES["a"]
+    n, H = 64, sh["hidden"]
+    lb = synth.make_layer(H, sh["experts"], sh["inter"], n, seed=4, dtype=torch.bfloat16)
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
+    buf = torch.empty(n * H + 2, dtype=torch.bfloat16, device="cuda")
+    x = buf[2:].view(n, H)
+    x.copy_(lb.x)
+    idx = torch.stack([torch.randperm(32)[:8] for _ in range(n)]).cuda()
+    gate = torch.full((n, 8), 0.125, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(MEPError, match="16-byte"):
+        be(x, idx, gate)
+    out = be(lb.x.cuda(), idx, gate)  # the context keeps working
+    assert torch.isfinite(out.float()).all()
+    be.comm.check()
+
+
 def test_router_bf16_rows_not_16_byte_aligned():
     """x starting 4 bytes past an allocation takes the CUDA-core kernel; its
     logits and selection obey the same contract as the staged kernel's."""
