@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--e2e-chunks", type=int, default=0,
                     help="pieces per host batch in the e2e leg (0: 4 from 4096 tokens per rank, else 2)")
     ap.add_argument("--force-simt", action="store_true")
+    ap.add_argument("--report", default=None,
+                    help="also write a bench report in the reference's results/bench_*.json layout")
     return ap.parse_args()
 
 
@@ -210,8 +212,9 @@ def run_reference(a):
 # --------------------------------------------------------------- GPU leg
 def main_b200(a):
     import torch.distributed as dist
-    from miniep_b200 import (Comm, EPMoEBackend, GraphedMoEBlock, Placement, StreamedMoEBlock, _lib,
-                             plan_balanced, straggler_overhead, synth)
+    from miniep_b200 import (Comm, EPMoEBackend, EPStats, GraphedMoEBlock, Placement,
+                             StreamedMoEBlock, _lib, plan_balanced, report, straggler_overhead,
+                             synth)
     from miniep_b200.ep import router_topk
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -251,7 +254,8 @@ def main_b200(a):
     w_in, w_out = lt.w_in[mine].contiguous(), lt.w_out[mine].contiguous()
     lt_router = lt.router.contiguous()
     del lt
-    be = EPMoEBackend(0, comm, placement, mine, w_in, w_out, None)
+    stats = EPStats(1, E)  # device counters; the report covers the timed graph steps only
+    be = EPMoEBackend(0, comm, placement, mine, w_in, w_out, stats)
 
     L, ctx = _lib.lib(), comm._ctx
     idx = torch.empty(n, k, dtype=torch.int64, device=dev)
@@ -322,6 +326,7 @@ def main_b200(a):
         blk()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
+    _lib.check(L.mep_reset_stats(ctx, st), ctx)
     clocks.start()
     wall0 = time.perf_counter()
     step_ms = timed(lambda i: blk(), a.steps)
@@ -333,6 +338,7 @@ def main_b200(a):
     if world > 1:
         dist.all_reduce(t_step, op=dist.ReduceOp.MAX)
     ms_step, ms_ffn, ms_eager = t_step.tolist()
+    snap = stats.snapshot()  # route counts and received entries of the timed steps
 
     # 3) e2e: the public graphed API with host buffers, copies inside the timed region
     e2e = None
@@ -433,6 +439,19 @@ def main_b200(a):
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
+    if a.report:
+        # every rank: its tokens, its counters, and (from the stage events) the
+        # time of its expert stage vs the rest of the step, over the timed steps
+        my_ffn, my_step = sum(ffn_ms) / n_eager, sum(step_ms) / a.steps
+        snap.update(compute_time=my_ffn * a.steps / 1e3,
+                    a2a_time=max(my_step - my_ffn, 0.0) * a.steps / 1e3, steps=a.steps)
+        got = report.gather_payloads(report.rank_payload(rank, n * a.steps, snap))
+        if rank == 0:
+            rep = report.bench_report(got, plan=a.plan, iters=a.steps, wall_time=wall,
+                                      iter_times=[t / 1e3 for t in step_ms])
+            report.write_bench_report(a.report, rep)
+            for line_ in report.summary_lines(rep):
+                print(line_, file=sys.stderr)
     del blk
     comm.close()
     if world > 1:

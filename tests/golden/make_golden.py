@@ -218,7 +218,11 @@ def gen_stats(ref_root: Path, out: Path):
         res[name] = dict(world=b["world"], recv_tokens_per_layer=loads.tolist(),
                          straggler=float(strag), imbalance_avg=float(per_layer.mean()),
                          imbalance_worst=float(per_layer.max()),
-                         snapshot_keys=sorted(b["ranks"][0]["stats"].keys()))
+                         snapshot_keys=sorted(b["ranks"][0]["stats"].keys()),
+                         bench_keys=list(b.keys()), rank_keys=list(b["ranks"][0].keys()),
+                         recv_tokens=[r["stats"]["recv_tokens"] for r in b["ranks"]],
+                         positions=[r["positions"] for r in b["ranks"]],
+                         wall_time=b["wall_time"], positions_per_s=b["positions_per_s"])
     nb = json.loads((ref_root / "results" / "bench_naive.json").read_text())
     bb = json.loads((ref_root / "results" / "bench_balanced.json").read_text())
     res["route_counts_placement_invariant"] = all(
