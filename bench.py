@@ -40,6 +40,10 @@ METRIC = "MoE layer tokens/s"
 UNIT = "tokens/s"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_BF16_TFLOPS = 1590.0
+# DRAM bytes (read + write) of the expert FFN stage (both tcgen05 launches) per
+# layer step, from one ncu capture of this bench at N=1 (profiles/
+# ffn_tc_shape_a_16k_dram.txt): keyed by (shape, tokens per step)
+FFN_DRAM_BYTES = {("a", 16384): 325.20e6 + 110.93e6 + 163.11e6 + 215.29e6}
 # router, routing (+ layout), dispatch, gemm1, gemm2, combine (+ data wait and fan-out when N > 1)
 KERNELS_PER_STEP = 6
 
@@ -398,6 +402,9 @@ def main_b200(a):
         if peak is None:
             peak, peak_src = FALLBACK_BF16_TFLOPS, "fallback"
         flops_rank0 = recv_rows * 6.0 * H * I  # algorithmic FLOPs of this rank's FFN launch
+        # GEMM1 reads rows (H) and writes act (I); GEMM2 reads act (I), writes rows (H);
+        # plus this rank's expert weights once per launch
+        n_local_w_bytes = len(mine) * 3.0 * H * I * 2
         achieved = flops_rank0 / (sum(ffn_ms) / n_eager / 1e3) / 1e12
         line = {
             "metric": METRIC, "value": a.tokens / (ms_step / 1e3), "unit": UNIT,
@@ -410,7 +417,11 @@ def main_b200(a):
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": peak_src,
                          "flops_per_launch": flops_rank0, "ms_per_launch": sum(ffn_ms) / n_eager,
-                         "traffic": None},
+                         "traffic": (FFN_DRAM_BYTES.get((a.shape, a.tokens)) if world == 1
+                                     else None),
+                         "traffic_unit": "bytes per launch (dram read + write, ncu)",
+                         "algorithmic_bytes": recv_rows * (2 * H + 2 * I) * 2.0
+                         + n_local_w_bytes},
             "ffn_ms_per_step_max_rank": ms_ffn,
             "eager": {"value": a.tokens / (ms_eager / 1e3), "ms_per_step": ms_eager,
                       "note": "same kernels launched one by one from Python"},

@@ -92,6 +92,42 @@ __device__ __forceinline__ void select_topk_warp(float v0, float v1, int k, int6
   }
 }
 
+// E <= 32: lane l holds expert l's model-dtype logit (-inf past E). A 32-lane
+// bitonic sort on (value descending, index ascending) -- the selection
+// order of the rounds above, ties to the lower index -- leaves the i-th
+// choice in lane i after 15 compare-exchange steps. The softmax then runs as
+// above: exp(v_i - v_0) on lanes < k, summed in slot order, one reciprocal.
+// Same values and summation order as select_topk_warp, so the same bits.
+template <typename T>
+__device__ __forceinline__ void select_topk_sort32(float v, int k, int64_t tok, int64_t* idx_out,
+                                                   T* gate_out) {
+  const int lane = lane_id();
+  int i = lane;
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int j = size >> 1; j > 0; j >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, j);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, j);
+      const bool other_better = ov > v || (ov == v && oi < i);
+      const bool lower = (lane & j) == 0;
+      const bool desc = (lane & size) == 0;  // this block ends best-first
+      if (lower == desc ? other_better : !other_better) {
+        v = ov;
+        i = oi;
+      }
+    }
+  }
+  const float top0 = __shfl_sync(0xffffffffu, v, 0);
+  const float e = lane < k ? expf(v - top0) : 0.f;
+  float ex_sum = 0.f;
+  for (int s = 0; s < k; ++s) ex_sum += __shfl_sync(0xffffffffu, e, s);
+  if (lane < k) {
+    idx_out[tok * k + lane] = i;
+    gate_out[tok * k + lane] = Elt<T>::from_f(e * (1.f / ex_sum));
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ float logit_to_model(float acc, const float* bias, int e) {
   float l = Elt<T>::round(acc);
@@ -190,7 +226,10 @@ __global__ void __launch_bounds__(128) k_router_bf16_mma(
         v[h2] = -INFINITY;
       }
     }
-    select_topk_warp<bf16>(v[0], v[1], k, tok, idx_out, gate_out);
+    if (NT <= 4)
+      select_topk_sort32<bf16>(v[0], k, tok, idx_out, gate_out);
+    else
+      select_topk_warp<bf16>(v[0], v[1], k, tok, idx_out, gate_out);
   }
 }
 
