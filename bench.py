@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--e2e-chunks", type=int, default=0,
                     help="pieces per host batch in the e2e leg (0: 4 from 4096 tokens per rank, else 2)")
     ap.add_argument("--force-simt", action="store_true")
+    ap.add_argument("--e2e-graph", choices=["on", "off"], default="off",
+                    help="capture the e2e host pipeline as one CUDA graph per step "
+                         "(measured slower at N=1 and 2: consecutive steps stop overlapping)")
     ap.add_argument("--report", default=None,
                     help="also write a bench report in the reference's results/bench_*.json layout")
     return ap.parse_args()
@@ -289,7 +292,11 @@ def main_b200(a):
         _lib.check(L.mep_combine(ctx, P(gate), None, n, P(h), rm, None, P(h_out), st), ctx)
 
     def timed(run, steps):
-        """Per-step device time (L2 flushed before each step, outside the events)."""
+        """Per-step device time (L2 flushed before each step, outside the events).
+        The region is bracketed by a host barrier and a synchronize; inside it
+        the ranks meet before every step in a device-side barrier (mep_barrier),
+        so no host wake-up latency lands inside a step and the host keeps the
+        queue ahead of the GPU."""
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         if world > 1:
@@ -298,7 +305,7 @@ def main_b200(a):
         for i in range(steps):
             flush_l2()
             if world > 1:
-                dist.barrier()
+                comm.barrier()
             starts[i].record()
             run(i)
             ends[i].record()
@@ -353,6 +360,9 @@ def main_b200(a):
 
         chunks = a.e2e_chunks or (4 if n >= 4096 else 2)
         sblk = StreamedMoEBlock(be, n, lt_router, rm, bias=bias, chunks=chunks)
+        graphed = a.e2e_graph == "on"
+        if graphed:
+            sblk.capture(x_host, h_host, out_host)  # one graph launch per step
 
         def e2e_step():
             sblk(x_host, h_host, out_host)
@@ -376,7 +386,9 @@ def main_b200(a):
                "d2h_bytes_per_step": out_host.numel() * 2,
                "ms_per_step": te.item(),
                "path": f"StreamedMoEBlock: x, h from pinned host memory in {chunks} pieces, "
-                       "copies overlapping the graphed steps"}
+                       "copies overlapping the pieces' steps"
+                       + (", one CUDA graph per step" if graphed else
+                          ", eager (consecutive steps overlap)")}
         comm.check()
     clk = clocks.stop()
 

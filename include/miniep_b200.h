@@ -186,6 +186,16 @@ int mep_check(mep_ctx* ctx);
 int mep_set_option(mep_ctx* ctx, const char* name, int64_t value);
 
 /*
+ * Rank barrier on the device: this rank's kernel raises its flag on every
+ * rank and waits (bounded by the context timeout) until every rank has done
+ * the same, so the streams of all ranks leave it together without a host
+ * round trip. No counterpart in the reference (its ranks meet in host
+ * collectives); used to start timed steps on all GPUs at the same moment.
+ * Every rank must call it the same number of times.
+ */
+int mep_barrier(mep_ctx* ctx, void* stream);
+
+/*
  * Test hook for bounded waits: launches one wait on this rank's counts flag
  * for `target`; if nothing raises it within timeout_ms the kernel records a
  * device error and returns, so the context stays usable.

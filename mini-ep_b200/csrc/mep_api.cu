@@ -180,7 +180,7 @@ int mep_ctx_create(int rank, int world, int device, int num_layers, int num_expe
 
   size_t off = 0;
   c->off_flags = off;
-  off = align_up(off + 3 * kMaxWorld * sizeof(uint32_t), 1024);
+  off = align_up(off + 4 * kMaxWorld * sizeof(uint32_t), 1024);
   c->off_cnt = off;
   off = align_up(off + (size_t)kMaxWorld * kMaxWorld * kMaxExperts * sizeof(int32_t), 1024);
   c->off_meta = off;
@@ -211,7 +211,7 @@ int mep_ctx_create(int rank, int world, int device, int num_layers, int num_expe
       {reinterpret_cast<void**>(&c->route_counts), (size_t)num_layers * num_experts * 8},
       {reinterpret_cast<void**>(&c->recv_per_layer), (size_t)num_layers * 8},
       {reinterpret_cast<void**>(&c->done_ctr), 4 * sizeof(unsigned int)},
-      {reinterpret_cast<void**>(&c->seq), sizeof(uint32_t)},
+      {reinterpret_cast<void**>(&c->seq), 2 * sizeof(uint32_t)},  // [0] layer step, [1] barrier
   };
   for (auto& a : allocs) {
     e = cudaMalloc(a.p, a.bytes);
@@ -532,6 +532,7 @@ int mep_check(mep_ctx* c) {
       "an entry was routed to a rank that does not hold its expert",
       "debug wait timed out",
       "a tensor-core pipeline barrier timed out",
+      "timed out waiting for a peer at a rank barrier",
   };
   const int nmsg = (int)(sizeof(msgs) / sizeof(msgs[0]));
   return fail(c, MEP_ERR_DEVICE,
@@ -554,6 +555,17 @@ int mep_set_option(mep_ctx* c, const char* name, int64_t value) {
     return MEP_OK;
   }
   return fail(c, MEP_ERR_INVALID, std::string("unknown option ") + name);
+}
+
+int mep_barrier(mep_ctx* c, void* stream) {
+  if (!c) return MEP_ERR_INVALID;
+  if (int rc = check_peers(c)) return rc;
+  if (int rc = use_device(c)) return rc;
+  launch_rank_barrier(c->peers, c->world, c->rank, c->seq + 1,
+                      reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), wait_cfg(c),
+                      as_stream(stream));
+  MEP_CK(c, cudaGetLastError());
+  return MEP_OK;
 }
 
 int mep_debug_wait(mep_ctx* c, uint32_t target, int64_t timeout_ms, void* stream) {

@@ -27,6 +27,7 @@ enum DevErr : int {
   kErrNotResident = 6,    // entry routed to a rank that does not hold the expert
   kErrWaitDebug = 7,      // the debug wait entry point timed out
   kErrPipeline = 8,       // a tensor-core pipeline barrier timed out
+  kErrWaitBarrier = 9,    // timed out waiting for a peer at a rank barrier
 };
 
 // Receive-side layout and send offsets for one layer step, computed on the
@@ -50,7 +51,7 @@ struct PeerPtrs {
   int32_t* recv_meta[kMaxWorld];
   void* yk[kMaxWorld];
   int32_t* cnt_in[kMaxWorld];
-  uint32_t* flags[kMaxWorld];  // [0,W) counts, [W,2W) data, [2W,3W) done
+  uint32_t* flags[kMaxWorld];  // [0,W) counts, [W,2W) data, [2W,3W) done, [3W,4W) barrier
 };
 
 struct WaitCfg {
@@ -86,6 +87,10 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
                      const void* x, const int64_t* topk_idx, const int32_t* ent_dest,
                      const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
                      unsigned int* done_ctr, const uint32_t* seq, int num_sms, cudaStream_t st);
+
+// every rank raises its barrier flag on every peer, then waits (bounded) for all
+void launch_rank_barrier(const PeerPtrs& peers, int world, int rank, uint32_t* bar_seq,
+                         const uint32_t* flags_local, WaitCfg wc, cudaStream_t st);
 
 // waits for flags [first, first + world) to reach *seq (or `target` when seq is null)
 // Receive rows that came from other ranks: copy each from the landing

@@ -157,6 +157,17 @@ __global__ void __launch_bounds__(256) k_fanout(int row_bytes, int topk, int ran
   }
 }
 
+// Rank barrier: raise barrier flag [3W + rank] on every rank to the next
+// barrier number, then wait for all W flags of this rank to reach it.
+__global__ void k_rank_barrier(PeerPtrs peers, int world, int rank, uint32_t* bar_seq,
+                               const uint32_t* flags, WaitCfg wc) {
+  const uint32_t s = *bar_seq + 1u;
+  if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + 3 * world + rank, s);
+  if (threadIdx.x < world) wait_flag(flags + 3 * world + threadIdx.x, s, kErrWaitBarrier, wc);
+  __syncthreads();
+  if (threadIdx.x == 0) *bar_seq = s;
+}
+
 __global__ void k_wait_flags(const uint32_t* flags, int first, int world, const uint32_t* seq,
                              uint32_t target, int code, WaitCfg wc) {
   const uint32_t step = seq ? *seq : target;
@@ -316,6 +327,11 @@ void launch_fanout(int dtype, int hidden, int topk, int rank, int64_t max_tokens
                                                   max_tokens, layout, recv_meta,
                                                   static_cast<const uint8_t*>(land),
                                                   static_cast<uint8_t*>(recv_x));
+}
+
+void launch_rank_barrier(const PeerPtrs& peers, int world, int rank, uint32_t* bar_seq,
+                         const uint32_t* flags_local, WaitCfg wc, cudaStream_t st) {
+  k_rank_barrier<<<1, 32, 0, st>>>(peers, world, rank, bar_seq, flags_local, wc);
 }
 
 void launch_wait_flags(const uint32_t* flags_local, int first, int world, const uint32_t* seq,

@@ -44,6 +44,7 @@ SIGNATURES = {
     "mep_check": [_P],
     "mep_set_option": [_P, C.c_char_p, _I64],
     "mep_debug_wait": [_P, C.c_uint32, _I64, _P],
+    "mep_barrier": [_P, _P],
     "mep_dest_ranks_noalloc": [_I, _I, _P, _P, _I, _P, _P, _I64, _P, _P],
 }
 _RESTYPES = {"mep_last_error": C.c_char_p}

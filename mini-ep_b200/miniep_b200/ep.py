@@ -171,6 +171,12 @@ class Comm:
         placement._comm = self
         self.placement = placement
 
+    def barrier(self):
+        """Rank barrier on the device (mep_barrier): enqueued on the current
+        stream; every rank's stream continues once all ranks have reached it.
+        Every rank must call it the same number of times."""
+        check(_lib.lib().mep_barrier(self._ctx, _stream()), self._ctx, "mep_barrier")
+
     def set_option(self, name: str, value: int):
         check(_lib.lib().mep_set_option(self._ctx, name.encode(), int(value)), self._ctx,
               "mep_set_option")
@@ -438,6 +444,9 @@ class StreamedMoEBlock:
     output row is bit-identical to the unchunked step's.
 
     Every rank must use the same ``chunks`` and call in lockstep.
+    ``capture`` records the whole pipeline for fixed pinned buffers into one
+    CUDA graph (consecutive calls then no longer overlap each other, only the
+    pieces of one call do).
     """
 
     def __init__(self, backend: "EPMoEBackend", n_tokens: int, router_w,
@@ -455,32 +464,67 @@ class StreamedMoEBlock:
         ev = lambda: [torch.cuda.Event() for _ in self.sizes]  # noqa: E731
         self.loaded, self.stepped, self.inputs_free, self.output_free = ev(), ev(), ev(), ev()
 
-    def __call__(self, x_host, h_host, out_host):
-        """Enqueue ``out_host = h_host + moe(x_host) * rm`` on the current
-        stream. The host tensors must be pinned for the copies to overlap;
-        ``out_host`` is complete once the current stream reaches this point."""
+    def _check(self, x_host, h_host, out_host):
         if x_host.shape[0] != self.n or h_host.shape[0] != self.n or out_host.shape[0] != self.n:
             raise ValueError(f"StreamedMoEBlock: expected {self.n} tokens")
+
+    def _enqueue(self, x_host, h_host, out_host, capturing: bool):
         cur = torch.cuda.current_stream()
+        if capturing:  # the side streams join the capture
+            self.copy_in.wait_stream(cur)
+            self.copy_out.wait_stream(cur)
         off = 0
         for i, (blk, m) in enumerate(zip(self.blocks, self.sizes)):
             rows = slice(off, off + m)
             off += m
             with torch.cuda.stream(self.copy_in):
-                self.copy_in.wait_event(self.inputs_free[i])  # last call's step i read blk.x / blk.h
+                if not capturing:
+                    self.copy_in.wait_event(self.inputs_free[i])  # last call's step i read blk.x / blk.h
                 blk.x.copy_(x_host[rows], non_blocking=True)
                 blk.h.copy_(h_host[rows], non_blocking=True)
                 self.loaded[i].record(self.copy_in)
             cur.wait_event(self.loaded[i])
-            cur.wait_event(self.output_free[i])  # last call's copy-out of blk.h_out is done
-            blk.graph.replay()
-            self.inputs_free[i].record(cur)
+            if capturing:
+                blk._step()
+            else:
+                cur.wait_event(self.output_free[i])  # last call's copy-out of blk.h_out is done
+                blk.graph.replay()
+                self.inputs_free[i].record(cur)
             self.stepped[i].record(cur)
             with torch.cuda.stream(self.copy_out):
                 self.copy_out.wait_event(self.stepped[i])
                 out_host[rows].copy_(blk.h_out, non_blocking=True)
-                self.output_free[i].record(self.copy_out)
+                if not capturing:
+                    self.output_free[i].record(self.copy_out)
+        if capturing:
+            cur.wait_stream(self.copy_in)
         cur.wait_stream(self.copy_out)
+
+    def capture(self, x_host, h_host, out_host):
+        """Record the whole per-call pipeline (copies in, the pieces' layer
+        steps, copies out, and their cross-stream order) into one CUDA graph
+        for these pinned host buffers; later calls with the same buffers
+        replay it: one launch per call instead of a few dozen. Every rank
+        captures at the same point."""
+        self._check(x_host, h_host, out_host)
+        self(x_host, h_host, out_host)  # one eager call first
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._enqueue(x_host, h_host, out_host, capturing=True)
+        self.graph = g
+        self.bound = (x_host.data_ptr(), h_host.data_ptr(), out_host.data_ptr())
+
+    def __call__(self, x_host, h_host, out_host):
+        """Enqueue ``out_host = h_host + moe(x_host) * rm`` on the current
+        stream. The host tensors must be pinned for the copies to overlap;
+        ``out_host`` is complete once the current stream reaches this point."""
+        self._check(x_host, h_host, out_host)
+        if getattr(self, "graph", None) is not None and self.bound == (
+                x_host.data_ptr(), h_host.data_ptr(), out_host.data_ptr()):
+            self.graph.replay()
+            return out_host
+        self._enqueue(x_host, h_host, out_host, capturing=False)
         return out_host
 
 

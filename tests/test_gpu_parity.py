@@ -399,4 +399,15 @@ def test_streamed_block_from_host_matches_unchunked_step():
         want, _, _ = be.moe_block(h_host.cuda(), x_host.cuda(), router,
                                   synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
         assert torch.equal(out_host, want.cpu())
+    # the whole pipeline as one graph over these buffers: new contents, same rows
+    blk.capture(x_host, h_host, out_host)
+    for part in (0, 1):
+        x_host.copy_(lb.x[part * n:(part + 1) * n])
+        h_host.copy_(hs[part * n:(part + 1) * n])
+        out_host.zero_()
+        blk(x_host, h_host, out_host)
+        torch.cuda.synchronize()
+        want, _, _ = be.moe_block(h_host.cuda(), x_host.cuda(), router,
+                                  synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
+        assert torch.equal(out_host, want.cpu())
     be.comm.check()
