@@ -329,7 +329,7 @@ int mep_dest_ranks(mep_ctx* c, int layer, const int64_t* expert_ids, int64_t m,
   if (int rc = use_device(c)) return rc;
   launch_dest_only(m, c->E, expert_ids, owners_of(c, layer), nrep_of(c, layer),
                    c->rr + (int64_t)layer * c->E, c->chunk_hist, c->ent_dest, c->ent_grp,
-                   c->my_counts, dest_out, wait_cfg(c), as_stream(stream));
+                   dest_out, wait_cfg(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   return MEP_OK;
 }

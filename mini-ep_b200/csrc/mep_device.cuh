@@ -76,9 +76,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
 __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -78,7 +78,7 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
 void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids,
                       const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,
                       int32_t* chunk_hist, int32_t* ent_dest, int32_t* ent_grp,
-                      int32_t* my_counts, int64_t* dest_out, WaitCfg wc, cudaStream_t st);
+                      int64_t* dest_out, WaitCfg wc, cudaStream_t st);
 
 
 // ---------------------------------------------------------------- movement

@@ -43,8 +43,7 @@ constexpr int64_t kNoAllocChunks = kNoAllocMaxIds / kRouteChunkTokens;
 constexpr size_t kOffHist = 0;
 constexpr size_t kOffDest = kOffHist + kNoAllocChunks * kMaxExperts * sizeof(int32_t);
 constexpr size_t kOffGrp = kOffDest + kNoAllocMaxIds * sizeof(int32_t);
-constexpr size_t kOffCounts = kOffGrp + kNoAllocMaxIds * sizeof(int32_t);
-constexpr size_t kOffOwners = kOffCounts + kMaxWorld * kMaxExperts * sizeof(int32_t);
+constexpr size_t kOffOwners = kOffGrp + kNoAllocMaxIds * sizeof(int32_t);
 constexpr size_t kOffNrep = kOffOwners + kMaxExperts * kMaxWorld * sizeof(int32_t);
 constexpr size_t kScratchBytes = kOffNrep + kMaxExperts * sizeof(int32_t);
 
@@ -126,8 +125,7 @@ extern "C" int mep_dest_ranks_noalloc(int num_experts, int world, const int64_t*
   launch_dest_only(m, num_experts, expert_ids, reinterpret_cast<const int32_t*>(s + kOffOwners),
                    reinterpret_cast<const int32_t*>(s + kOffNrep), rr,
                    reinterpret_cast<int32_t*>(s + kOffHist), reinterpret_cast<int32_t*>(s + kOffDest),
-                   reinterpret_cast<int32_t*>(s + kOffGrp),
-                   reinterpret_cast<int32_t*>(s + kOffCounts), dest_out, WaitCfg{nullptr, 0}, st);
+                   reinterpret_cast<int32_t*>(s + kOffGrp), dest_out, WaitCfg{nullptr, 0}, st);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "kernel launch");
   return MEP_OK;

@@ -131,53 +131,25 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_rank(
   }
 }
 
-// Totals, round-robin state, stats, per-(destination, expert) counts; when
-// `publish`, the counts are stored into every rank's exchange slot for this
-// source and the rank's counts flag is raised. The round-robin state of a
-// layer without any replicated expert is left alone, like the reference's
-// fast path (ep.py:84-85); it cannot affect any destination there.
-__global__ void __launch_bounds__(256) k_route_finalize(
-    int nchunks, int E, int world, int rank, const int32_t* __restrict__ owners,
-    const int32_t* __restrict__ nrep, int64_t* __restrict__ rr, int64_t* __restrict__ route_counts,
-    const int32_t* __restrict__ chunk_hist, int32_t* __restrict__ my_counts, PeerPtrs peers,
-    uint32_t* seq, int publish) {
-  __shared__ int cnt[kMaxWorld * kMaxExperts];
-  // this layer step's sequence number: one past the previous step's (kept on
-  // the device so that a captured graph of the step stays valid on replay)
-  const uint32_t step = publish ? *seq + 1u : 0u;
+// Round-robin state after a destination scan (mep_dest_ranks): rr[e] +=
+// count[e], except on a layer without any replicated expert, whose state the
+// reference's fast path (ep.py:84-85) leaves alone.
+__global__ void __launch_bounds__(256) k_route_rr_advance(int nchunks, int E,
+                                                          const int32_t* __restrict__ nrep,
+                                                          int64_t* __restrict__ rr,
+                                                          const int32_t* __restrict__ chunk_hist) {
   __shared__ int any_rep;
   if (threadIdx.x == 0) any_rep = 0;
-  for (int i = threadIdx.x; i < world * E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x)
     if (nrep[e] > 1) any_rep = 1;
   __syncthreads();
+  if (!any_rep) return;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int c = 0;
     for (int ch = 0; ch < nchunks; ++ch) c += chunk_hist[(int64_t)ch * E + e];
-    const int nr = nrep[e];
-    const int rr0 = (int)(rr[e] % nr);
-    for (int j = 0; j < nr; ++j) {
-      const int d = owners[e * kMaxWorld + j];
-      const int w0 = ((j - rr0) % nr + nr) % nr;
-      cnt[d * E + e] = c > w0 ? (c - w0 - 1) / nr + 1 : 0;
-    }
-    if (any_rep) rr[e] += c;
-    if (route_counts) route_counts[e] += c;
+    rr[e] += c;
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < world * E; i += blockDim.x) my_counts[i] = cnt[i];
-  if (!publish) return;
-  for (int d = 0; d < world; ++d) {
-    int32_t* dst = peers.cnt_in[d] + (int64_t)rank * world * E;
-    for (int i = threadIdx.x; i < world * E; i += blockDim.x) dst[i] = cnt[i];
-  }
-  __syncthreads();  // every thread's count stores happen before the fence below
-  if (threadIdx.x == 0) __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, step);
-  __syncthreads();
-  if (threadIdx.x == 0) *seq = step;
 }
 
 // Receive layout + send offsets from the exchanged counts C[s][d][e], by one
@@ -249,7 +221,8 @@ __device__ void layout_block(int world, int rank, int E, const int32_t* __restri
 }
 
 // ---------------------------------------------------------------------------
-// The three routing passes above as ONE launch, for the layer step.
+// The routing passes as ONE launch, for the layer step (the two-kernel scan
+// above serves the stand-alone destination scan, mep_dest_ranks).
 //
 // grid G <= number of SMs (one 256-thread CTA per SM at most, so every CTA of
 // the grid is resident at once); CTA b owns tokens [b*tpc, (b+1)*tpc), tpc a
@@ -348,7 +321,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   __syncthreads();
 
   if (b == 0) {
-    // finalize (k_route_finalize's work): counts per (dest, expert), rr, stats, publish
+    // finalize: counts per (dest, expert), rr, stats, publish
     const uint32_t step = *seq + 1u;
     for (int i = threadIdx.x; i < world * E; i += blockDim.x) cnt[i] = 0;
     for (int e = threadIdx.x; e < E; e += blockDim.x)
@@ -464,8 +437,8 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
 
 void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids, const int32_t* owners_l,
                       const int32_t* nrep_l, int64_t* rr_l, int32_t* chunk_hist,
-                      int32_t* ent_dest, int32_t* ent_grp, int32_t* my_counts, int64_t* dest_out,
-                      WaitCfg wc, cudaStream_t st) {
+                      int32_t* ent_dest, int32_t* ent_grp, int64_t* dest_out, WaitCfg wc,
+                      cudaStream_t st) {
   const int nchunks = (int)((m + kRouteChunkTokens - 1) / kRouteChunkTokens);
   if (nchunks > 0) {
     k_route_hist<<<nchunks, kRouteThreads, 0, st>>>(m, 1, experts, expert_ids, nullptr, chunk_hist,
@@ -474,9 +447,7 @@ void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids, const i
                                                     nrep_l, rr_l, chunk_hist, ent_dest, ent_grp);
     k_dest_to_i64<<<(unsigned)((m + 255) / 256), 256, 0, st>>>(m, ent_dest, dest_out);
   }
-  PeerPtrs none{};
-  k_route_finalize<<<1, 256, 0, st>>>(nchunks, experts, kMaxWorld, 0, owners_l, nrep_l, rr_l,
-                                      nullptr, chunk_hist, my_counts, none, nullptr, 0);
+  k_route_rr_advance<<<1, 256, 0, st>>>(nchunks, experts, nrep_l, rr_l, chunk_hist);
 }
 
 
