@@ -162,7 +162,7 @@ def cpu_step(oracle, lb, bias, h, k):
     return out
 
 
-def cpu_baseline(sh, sample_tokens, min_seconds=10.0, max_reps=20) -> dict:
+def cpu_baseline(sh, sample_tokens, min_seconds=10.0, max_reps=2000) -> dict:
     """The CPU checker's restatement of the reference path (router +
     LocalMoEBackend + residual) on this host's cores, on a bounded sample."""
     from oracle import moe_oracle
