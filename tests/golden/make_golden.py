@@ -21,6 +21,12 @@ the tests that use them never need the reference at run time. What is pinned:
                                known answer plus synthetic skewed count matrices.
 * ``stats_schema.json``       EPStats.snapshot keys and the straggler figures
                                recomputed from the shipped bench results.
+* ``model_tiny.npz``          GraniteMoeModel (modeling.py:148-262) with
+                               LocalMoEBackend, driven like the engine's
+                               prefill + greedy decode (worker.py:38-138) over a
+                               right-padded shard of three prompts, fp32, on a
+                               two-layer model with synthetic weights
+                               (miniep_b200.model.random_weights).
 """
 from __future__ import annotations
 
@@ -208,6 +214,57 @@ def gen_balancer(ref_root: Path, out: Path):
     (out / "balancer.json").write_text(json.dumps(cases))
 
 
+MODEL_TINY = dict(
+    hidden_size=256, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+    num_key_value_heads=2, num_local_experts=8, num_experts_per_tok=2, vocab_size=512,
+    rms_norm_eps=1e-6, rope_theta=10000.0, embedding_multiplier=12.0,
+    attention_multiplier=0.015625, residual_multiplier=0.22, logits_scaling=6.0,
+    max_position_embeddings=256)
+MODEL_TINY_PROMPT_LENS = (7, 12, 4)
+MODEL_TINY_NEW = 6
+
+
+def gen_model(out: Path):
+    from miniep.modeling import GraniteMoeModel, LocalMoEBackend, ModelConfig
+    from miniep.worker import Shard
+    from miniep_b200.model import ModelConfig as Cfg, expert_weight_keys, random_weights
+    cfg = ModelConfig(**MODEL_TINY)
+    w = random_weights(Cfg.from_dict(MODEL_TINY), seed=5, dtype=torch.float32)
+    backends = [LocalMoEBackend(w[a], w[b]) for a, b in map(expert_weight_keys, range(2))]
+    model = GraniteMoeModel(cfg, w, backends)
+    g = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(1, cfg.vocab_size, (n,), generator=g).tolist()
+               for n in MODEL_TINY_PROMPT_LENS]
+    shard = Shard(prompts, cfg.num_hidden_layers, pad_id=cfg.pad_token_id)
+    with torch.no_grad():
+        # Engine.prefill (worker.py:100-112)
+        mask, moe_valid = shard.prefill_masks()
+        logits = model(shard.input, kv_cache=shard.kv, attn_mask=mask, moe_valid=moe_valid,
+                       logits_at=shard.lengths - 1)
+        prefill = logits[:, 0].clone()
+        shard.last_tokens = prefill.argmax(dim=-1)
+        steps = []
+        # Engine.decode_step (worker.py:126-138), all rows active
+        for _ in range(MODEL_TINY_NEW):
+            for i in range(shard.B):
+                shard.generated[i].append(int(shard.last_tokens[i]))
+            mask, _ = shard.decode_masks()
+            logits = model(shard.last_tokens.unsqueeze(1), positions=shard.positions_decode(),
+                           kv_cache=shard.kv, attn_mask=mask)
+            steps.append(logits[:, -1].clone())
+            shard.last_tokens = logits[:, -1].argmax(dim=-1)
+            shard.decoded_steps += 1
+    allv = torch.cat([prefill[None], torch.stack(steps)])  # (1+steps, B, V)
+    top2 = allv.topk(2, dim=-1).values
+    gap = float((top2[..., 0] - top2[..., 1]).min())
+    assert gap > 1e-3, f"greedy choice too close to a tie ({gap})"
+    np.savez_compressed(out / "model_tiny.npz", config=json.dumps(MODEL_TINY),
+                        prompt_lens=np.array(MODEL_TINY_PROMPT_LENS),
+                        prompts=np.array(sum(prompts, [])), generated=np.array(shard.generated),
+                        prefill_logits=prefill.numpy(), decode_logits=torch.stack(steps).numpy(),
+                        min_top2_gap=gap)
+
+
 def gen_stats(ref_root: Path, out: Path):
     res = {}
     for name in ("naive", "balanced"):
@@ -245,6 +302,7 @@ def main():
         "dest_ranks": lambda: gen_dest_ranks(ref_root, HERE),
         "balancer": lambda: gen_balancer(ref_root, HERE),
         "stats": lambda: gen_stats(ref_root, HERE),
+        "model": lambda: gen_model(HERE),
     }
     for name, fn in steps.items():
         if args.only and name not in args.only.split(","):
