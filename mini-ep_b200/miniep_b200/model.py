@@ -236,10 +236,34 @@ class DeviceModel:
             shard.v[l, :, :, col0:col0 + T] = v
             keys = shard.k[l, :, :, :col0 + T]
             vals = shard.v[l, :, :, :col0 + T]
-        with sdpa_kernel(_SDPA):
-            o = F.scaled_dot_product_attention(q, keys, vals, attn_mask=mask,
-                                               scale=cfg.attention_multiplier, enable_gqa=True)
+        o = self._sdpa(q, keys, vals, mask)
         return o.transpose(1, 2).reshape(B, T, H) @ self.w[p + "o_proj.weight"].T
+
+    def _sdpa(self, q, k, v, mask):
+        """Attention of q (B, Hq, T, D) over k, v (B, Hk, S, D), query head h
+        on KV head h // (Hq / Hk).
+
+        mask None (prefill, keys = the T prompt columns): causal. For every
+        query inside its row's prompt the causal keys are exactly the valid
+        ones (padding sits after the prompt), so this equals the reference's
+        causal-and-valid mask there; padded positions are never read (their
+        expert entries are masked and decode masks their cache columns).
+        mask (B, 1, 1, S) (decode: depends on the key only): the query heads of
+        one KV head are folded into that head's query rows, plain attention
+        with a broadcast mask, no GQA support needed from the kernel."""
+        cfg = self.cfg
+        if mask is None:
+            with sdpa_kernel(_SDPA):
+                return F.scaled_dot_product_attention(q, k, v, is_causal=True,
+                                                      scale=cfg.attention_multiplier,
+                                                      enable_gqa=True)
+        B, Hq, T, D = q.shape
+        Hk = k.shape[1]
+        qg = q.reshape(B, Hk, (Hq // Hk) * T, D)
+        with sdpa_kernel(_SDPA):
+            o = F.scaled_dot_product_attention(qg, k, v, attn_mask=mask,
+                                               scale=cfg.attention_multiplier)
+        return o.reshape(B, Hq, T, D)
 
     def forward(self, ids, positions, shard: Shard, col0: int, mask, moe_valid, logits_at=None):
         cfg = self.cfg
@@ -274,11 +298,11 @@ class Engine:
     @torch.no_grad()
     def prefill(self, shard: Shard, dummy: bool = False):
         self.reset_rr()
-        mask, valid = shard.prefill_masks()
+        _, valid = shard.prefill_masks()
         if dummy:
             valid = torch.zeros_like(valid)
         pos = torch.arange(shard.T, device=shard.input.device).unsqueeze(0).expand(shard.B, -1)
-        logits = self.model.forward(shard.input, pos, shard, 0, mask, valid,
+        logits = self.model.forward(shard.input, pos, shard, 0, None, valid,
                                     logits_at=shard.lengths - 1)
         shard.used = shard.T
         self.steps += 1
