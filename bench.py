@@ -1,5 +1,6 @@
-"""MoE-layer throughput on B200: one expert-parallel GraniteMoE-shaped layer step
-(router + route + dispatch + grouped SwiGLU experts + combine + residual).
+"""MoE-layer throughput on B200: one expert-parallel GraniteMoE-shaped MoE block
+step from the residual stream h (post-attention RMSNorm + router + route +
+dispatch + grouped SwiGLU experts + combine + residual, modeling.py:192-197).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
@@ -14,8 +15,9 @@ Prints one JSON line (rank 0). `value` is whole-job tokens/s of the device
 step (inputs resident in HBM, L2 flushed between steps, per-step CUDA events,
 max over ranks); `e2e` is the same metric through the public API with the
 step's inputs copied from pinned host memory and its output copied back
-inside the timed region. `--impl reference` times the CPU checker's
-restatement of the reference's LocalMoEBackend + router on this host's cores.
+inside the timed region (h is the block's only input). `--impl reference`
+times the CPU checker's restatement of the reference's block (RMSNorm,
+router, LocalMoEBackend, residual) on this host's cores.
 """
 from __future__ import annotations
 
@@ -44,8 +46,8 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # layer step, from one ncu capture of this bench at N=1 (profiles/
 # ffn_tc_shape_a_16k_dram.txt): keyed by (shape, tokens per step)
 FFN_DRAM_BYTES = {("a", 16384): 325.20e6 + 110.93e6 + 163.11e6 + 215.29e6}
-# router, routing (+ layout), dispatch, gemm1, gemm2, combine (+ data wait and fan-out when N > 1)
-KERNELS_PER_STEP = 6
+# norm, router, routing (+ layout), dispatch, gemm1, gemm2, combine (+ data wait and fan-out when N > 1)
+KERNELS_PER_STEP = 7
 
 
 def parse():
@@ -78,6 +80,8 @@ def workload_name(a) -> str:
 def config(a, sh) -> dict:
     return {"workload": workload_name(a), "tokens_per_step": a.tokens, "hidden": sh["hidden"],
             "experts": sh["experts"], "topk": sh["topk"], "inter": sh["inter"],
+            "block": "post-attention RMSNorm + router + experts + residual from h "
+                     "(modeling.py:192-197)",
             "router": "zipf(1.2) bias x2.0, layer 0", "placement": a.plan,
             "l2": "flushed between timed steps (512 MiB write + 256 MiB read, outside the step events)"}
 
@@ -155,10 +159,20 @@ def cpu_sample_inputs(sh, n_tokens, seed=0):
     return lb, bias, h
 
 
+NORM_EPS = 1e-6
+
+
+def norm_weight(hidden: int, device=None):
+    """Synthetic post-attention RMSNorm weight: 1 + N(0, 1) * 0.02 (seed 8)."""
+    g = torch.Generator().manual_seed(8)
+    return (1.0 + 0.02 * torch.randn(hidden, generator=g)).to(torch.bfloat16).to(device)
+
+
 def cpu_step(oracle, lb, bias, h, k):
     from miniep_b200 import synth
-    out, _, _ = oracle.moe_block(h, lb.x, lb.router, lb.w_in, lb.w_out, k,
-                                 synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
+    out, _, _, _ = oracle.moe_block_from_h(h, norm_weight(h.shape[1]), NORM_EPS, lb.router,
+                                           lb.w_in, lb.w_out, k,
+                                           synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
     return out
 
 
@@ -180,7 +194,7 @@ def cpu_baseline(sh, sample_tokens, min_seconds=10.0, max_reps=2000) -> dict:
     return {"value": reps * sample_tokens / dt, "unit": UNIT, "cores": torch.get_num_threads(),
             "kind": "port",
             "sample": f"{reps} x {sample_tokens} tokens of the same workload (bf16, shape, "
-                      f"Zipf router) through oracle.moe_block, {dt:.1f} s"}
+                      f"Zipf router) through oracle.moe_block_from_h, {dt:.1f} s"}
 
 
 def run_reference(a):
@@ -209,7 +223,7 @@ def run_reference(a):
         "data": "synthetic", "config": config(a, sh),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{sample} tokens per step through oracle.moe_block "
+                         "sample": f"{sample} tokens per step through oracle.moe_block_from_h "
                                    f"(router + LocalMoEBackend + residual restated in torch CPU)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -222,7 +236,7 @@ def main_b200(a):
     from miniep_b200 import (Comm, EPMoEBackend, EPStats, GraphedMoEBlock, Placement,
                              StreamedMoEBlock, _lib, plan_balanced, report, straggler_overhead,
                              synth)
-    from miniep_b200.ep import router_topk
+    from miniep_b200.ep import rms_norm, router_topk
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -240,8 +254,8 @@ def main_b200(a):
     # same weights on every rank (same seed), each rank its own token shard
     lt = synth.make_layer(H, E, I, a.tokens, seed=0, dtype=torch.bfloat16, device=dev)
     bias = synth.zipf_router_bias(1, E)[0].to(dev)
-    x = lt.x[start:stop].contiguous()
     h = synth.make_tokens(a.tokens, H, seed=7, dtype=torch.bfloat16, device=dev)[start:stop].contiguous()
+    nw = norm_weight(H, dev)
     rm = synth.GRANITE_RESIDUAL_MULTIPLIER
 
     comm = Comm(num_layers=1, num_experts=E, topk=k, hidden=H, inter=I, max_tokens=n,
@@ -252,7 +266,7 @@ def main_b200(a):
     counts = None
     if world > 1 and a.plan == "balanced":
         comm.install(placement)
-        idx, _ = router_topk(comm, x, lt.router, bias)
+        idx, _ = router_topk(comm, rms_norm(comm, h, nw, NORM_EPS), lt.router, bias)
         counts = torch.bincount(idx.reshape(-1), minlength=E).to(torch.int64)
         dist.all_reduce(counts)
         placement, _ = plan_balanced(counts.view(1, E).cpu(), world, slots_per_rank=2)
@@ -278,8 +292,11 @@ def main_b200(a):
         flush.zero_()
         flush_rd.sum()
 
+    x = torch.empty_like(h)
+
     def eager_step(st, ev_ffn=None):
-        # mep_moe_block's sequence, with events around the expert FFN stage
+        # mep_moe_block_from_h's sequence, with events around the expert FFN stage
+        _lib.check(L.mep_rmsnorm(ctx, P(h), P(nw), NORM_EPS, n, P(x), st), ctx)
         _lib.check(L.mep_router_topk(ctx, P(x), P(lt_router), P(bias), n, P(idx), P(gate),
                                      None, st), ctx)
         _lib.check(L.mep_route(ctx, 0, P(idx), None, n, len(mine), st), ctx)
@@ -330,8 +347,7 @@ def main_b200(a):
     comm.check()
 
     # 2) the step as one CUDA graph (GraphedMoEBlock): the reported value
-    blk = GraphedMoEBlock(be, n, lt_router, rm, bias=bias)
-    blk.x.copy_(x)
+    blk = GraphedMoEBlock(be, n, lt_router, rm, bias=bias, norm_w=nw, eps=NORM_EPS)
     blk.h.copy_(h)
     for _ in range(a.warmup):
         blk()
@@ -354,18 +370,18 @@ def main_b200(a):
     # 3) e2e: the public graphed API with host buffers, copies inside the timed region
     e2e = None
     if not a.no_e2e:
-        x_host = x.cpu().pin_memory()
         h_host = h.cpu().pin_memory()
         out_host = torch.empty_like(h_host).pin_memory()
 
         chunks = a.e2e_chunks or (4 if n >= 4096 else 2)
-        sblk = StreamedMoEBlock(be, n, lt_router, rm, bias=bias, chunks=chunks)
+        sblk = StreamedMoEBlock(be, n, lt_router, rm, bias=bias, chunks=chunks, norm_w=nw,
+                                eps=NORM_EPS)
         graphed = a.e2e_graph == "on"
         if graphed:
-            sblk.capture(x_host, h_host, out_host)  # one graph launch per step
+            sblk.capture(None, h_host, out_host)  # one graph launch per step
 
         def e2e_step():
-            sblk(x_host, h_host, out_host)
+            sblk(None, h_host, out_host)
 
         for _ in range(max(1, a.warmup)):
             e2e_step()
@@ -382,10 +398,10 @@ def main_b200(a):
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e = {"value": a.tokens / (te.item() / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": (x_host.numel() + h_host.numel()) * 2,
+               "h2d_bytes_per_step": h_host.numel() * 2,
                "d2h_bytes_per_step": out_host.numel() * 2,
                "ms_per_step": te.item(),
-               "path": f"StreamedMoEBlock: x, h from pinned host memory in {chunks} pieces, "
+               "path": f"StreamedMoEBlock: h from pinned host memory in {chunks} pieces, "
                        "copies overlapping the pieces' steps"
                        + (", one CUDA graph per step" if graphed else
                           ", eager (consecutive steps overlap)")}

@@ -139,6 +139,28 @@ int mep_moe_block(mep_ctx* ctx, int layer, const void* h, const void* x, const v
                   int64_t* topk_idx_out, void* topk_gate_out, void* stream);
 
 /*
+ * Post-attention RMSNorm of the MoE block: x = w * (h * rsqrt(mean(h^2) + eps)),
+ * in the model dtype with the reference's rounding points.
+ *   replaces: rms_norm (miniep/modeling.py:51-52) as called at :192
+ * h, x: (n, H) rows starting on 16-byte boundaries; w: (H,).
+ */
+int mep_rmsnorm(mep_ctx* ctx, const void* h, const void* w, float eps, int64_t n, void* x_out,
+                void* stream);
+
+/*
+ * The MoE half of Block.forward from the residual stream alone: x = rms_norm(h),
+ * router, MoE layer step, h_out = h + moe(x) * residual_multiplier.
+ *   replaces: Block.forward lines miniep/modeling.py:192-197
+ * x_out: (n, H) device scratch the caller owns (receives the normalised rows);
+ * topk_idx_out / topk_gate_out as for mep_moe_block.
+ */
+int mep_moe_block_from_h(mep_ctx* ctx, int layer, const void* h, const void* norm_w, float eps,
+                         const void* router_w, const float* bias, const uint8_t* valid,
+                         int64_t n, const void* w_in, const void* w_out, int n_local,
+                         float residual_multiplier, void* h_out, void* x_out,
+                         int64_t* topk_idx_out, void* topk_gate_out, void* stream);
+
+/*
  * The layer step as separately launchable stages, in this order, for stage
  * timing and profiling (mep_moe_forward runs exactly these):
  *   mep_route       flatten_topk + route_counts + dest_ranks + counts publish

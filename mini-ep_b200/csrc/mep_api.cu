@@ -484,6 +484,31 @@ int mep_moe_block(mep_ctx* c, int layer, const void* h, const void* x, const voi
   return mep_combine(c, topk_gate_out, valid, n, h, residual_multiplier, nullptr, h_out, stream);
 }
 
+int mep_rmsnorm(mep_ctx* c, const void* h, const void* w, float eps, int64_t n, void* x_out,
+                void* stream) {
+  if (!c) return MEP_ERR_INVALID;
+  if (n < 0) return fail(c, MEP_ERR_INVALID, "n must be >= 0");
+  if (n > 0 && (!h || !w || !x_out)) return fail(c, MEP_ERR_INVALID, "NULL argument");
+  if (n > 0 && ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(w) |
+                 reinterpret_cast<uintptr_t>(x_out)) & 15u) != 0)
+    return fail(c, MEP_ERR_INVALID, "h, w and x_out must start on 16-byte boundaries");
+  if (!(eps >= 0.f)) return fail(c, MEP_ERR_INVALID, "eps must be >= 0");
+  if (int rc = use_device(c)) return rc;
+  launch_rmsnorm(c->dtype, n, c->H, h, w, eps, x_out, as_stream(stream));
+  MEP_CK(c, cudaGetLastError());
+  return MEP_OK;
+}
+
+int mep_moe_block_from_h(mep_ctx* c, int layer, const void* h, const void* norm_w, float eps,
+                         const void* router_w, const float* bias, const uint8_t* valid,
+                         int64_t n, const void* w_in, const void* w_out, int n_local,
+                         float residual_multiplier, void* h_out, void* x_out,
+                         int64_t* topk_idx_out, void* topk_gate_out, void* stream) {
+  if (int rc = mep_rmsnorm(c, h, norm_w, eps, n, x_out, stream)) return rc;
+  return mep_moe_block(c, layer, h, x_out, router_w, bias, valid, n, w_in, w_out, n_local,
+                       residual_multiplier, h_out, topk_idx_out, topk_gate_out, stream);
+}
+
 int mep_read_stats(mep_ctx* c, int64_t* route_counts_out, int64_t* recv_out, void* stream) {
   if (!c) return MEP_ERR_INVALID;
   if (int rc = use_device(c)) return rc;

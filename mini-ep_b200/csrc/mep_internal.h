@@ -64,6 +64,10 @@ void launch_router(int dtype, const void* x, const void* router_w, const float* 
                    int64_t n, int hidden, int experts, int topk, int64_t* idx_out,
                    void* gate_out, float* logits_out, int num_sms, int* err, cudaStream_t st);
 
+// ---------------------------------------------------------------- RMSNorm
+void launch_rmsnorm(int dtype, int64_t n, int hidden, const void* h, const void* w, float eps,
+                    void* x, cudaStream_t st);
+
 // ---------------------------------------------------------------- routing
 void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   const int64_t* topk_idx, const uint8_t* valid,

@@ -34,6 +34,9 @@ SIGNATURES = {
     "mep_router_topk": [_P, _P, _P, _P, _I64, _P, _P, _P, _P],
     "mep_moe_forward": [_P, _I, _P, _P, _P, _P, _I64, _P, _P, _I, _P, _P],
     "mep_moe_block": [_P, _I, _P, _P, _P, _P, _P, _I64, _P, _P, _I, C.c_float, _P, _P, _P, _P],
+    "mep_rmsnorm": [_P, _P, _P, C.c_float, _I64, _P, _P],
+    "mep_moe_block_from_h": [_P, _I, _P, _P, C.c_float, _P, _P, _P, _I64, _P, _P, _I, C.c_float,
+                             _P, _P, _P, _P, _P],
     "mep_route": [_P, _I, _P, _P, _I64, _I, _P],
     "mep_dispatch": [_P, _P, _P, _I64, _P],
     "mep_expert_ffn": [_P, _P, _P, _I, _P],

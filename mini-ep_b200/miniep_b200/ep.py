@@ -373,6 +373,30 @@ class EPMoEBackend:
                                        ptr(gate), _stream()), comm._ctx, "mep_moe_block")
         return h_out.view_as(h), idx, gate
 
+    def moe_block_from_h(self, h, norm_w, eps: float, router_w, residual_multiplier: float,
+                         bias=None, valid_mask=None):
+        """The MoE half of ``Block.forward`` from the residual stream alone
+        (miniep/modeling.py:192-197): post-attention RMSNorm, router, this
+        backend, residual, in one call. Returns (h_out, topk_idx, topk_gate, x)."""
+        comm = self.comm
+        n = h.reshape(-1, comm.hidden).shape[0]
+        hh = h.reshape(n, -1).contiguous()
+        n_local = self._prepare(hh)
+        nw = norm_w.to(device=hh.device, dtype=comm.dtype).contiguous()
+        rw = router_w.to(comm.dtype).contiguous()
+        b = None if bias is None else bias.to(device=hh.device, dtype=torch.float32).contiguous()
+        valid = _as_valid(valid_mask, n, hh.device)
+        x = torch.empty_like(hh)
+        idx = torch.empty(n, comm.topk, dtype=torch.int64, device=hh.device)
+        gate = torch.empty(n, comm.topk, dtype=comm.dtype, device=hh.device)
+        h_out = torch.empty_like(hh)
+        w_in, w_out = self.w_in.contiguous(), self.w_out.contiguous()
+        check(_lib.lib().mep_moe_block_from_h(
+            comm._ctx, self.layer, ptr(hh), ptr(nw), float(eps), ptr(rw), ptr(b), ptr(valid), n,
+            ptr(w_in), ptr(w_out), n_local, float(residual_multiplier), ptr(h_out), ptr(x),
+            ptr(idx), ptr(gate), _stream()), comm._ctx, "mep_moe_block_from_h")
+        return h_out.view_as(h), idx, gate, x
+
 
 class GraphedMoEBlock:
     """The MoE half of ``Block.forward`` (router + expert-parallel layer +
@@ -387,7 +411,7 @@ class GraphedMoEBlock:
     """
 
     def __init__(self, backend: "EPMoEBackend", n_tokens: int, router_w,
-                 residual_multiplier: float, bias=None):
+                 residual_multiplier: float, bias=None, norm_w=None, eps: float = 1e-6):
         comm = backend.comm
         self.backend, self.n = backend, n_tokens
         dev = backend.w_in.device
@@ -400,6 +424,11 @@ class GraphedMoEBlock:
         self.router_w = router_w.to(comm.dtype).contiguous()
         self.bias = None if bias is None else bias.to(device=dev, dtype=torch.float32).contiguous()
         self.rm = float(residual_multiplier)
+        # with the post-attention norm weight the block starts from h alone:
+        # x is computed on the device (modeling.py:192)
+        self.norm_w = None if norm_w is None else \
+            norm_w.to(device=dev, dtype=comm.dtype).contiguous()
+        self.eps = float(eps)
         self.n_local = backend._prepare(self.x)
         self._step()  # warm-up outside capture (resolves driver entry points, kernel attributes)
         torch.cuda.current_stream().synchronize()
@@ -411,6 +440,9 @@ class GraphedMoEBlock:
     def _step(self):
         be, comm = self.backend, self.backend.comm
         L, ctx, st, n = _lib.lib(), comm._ctx, _stream(), self.n
+        if self.norm_w is not None:
+            check(L.mep_rmsnorm(ctx, ptr(self.h), ptr(self.norm_w), self.eps, n, ptr(self.x), st),
+                  ctx, "mep_rmsnorm")
         check(L.mep_router_topk(ctx, ptr(self.x), ptr(self.router_w), ptr(self.bias), n,
                                 ptr(self.idx), ptr(self.gate), None, st), ctx, "mep_router_topk")
         check(L.mep_route(ctx, be.layer, ptr(self.idx), None, n, self.n_local, st), ctx, "mep_route")
@@ -422,7 +454,10 @@ class GraphedMoEBlock:
 
     def __call__(self, x=None, h=None):
         """Copy x / h (device or pinned host tensors) into the static inputs
-        when given, replay the step, return the static output h + moe(x) * rm."""
+        when given, replay the step, return the static output h + moe(x) * rm.
+        With the norm weight the step computes x from h; pass h only."""
+        if x is not None and self.norm_w is not None:
+            raise ValueError("this block computes x from h (norm_w given): pass h only")
         if x is not None:
             self.x.copy_(x, non_blocking=True)
         if h is not None:
@@ -450,14 +485,17 @@ class StreamedMoEBlock:
     """
 
     def __init__(self, backend: "EPMoEBackend", n_tokens: int, router_w,
-                 residual_multiplier: float, bias=None, chunks: int = 4):
+                 residual_multiplier: float, bias=None, chunks: int = 4, norm_w=None,
+                 eps: float = 1e-6):
         if n_tokens < 1 or chunks < 1:
             raise ValueError("StreamedMoEBlock: n_tokens and chunks must be positive")
         chunks = min(chunks, n_tokens)
         base, extra = divmod(n_tokens, chunks)
         self.sizes = [base + (1 if i < extra else 0) for i in range(chunks)]
         self.n = n_tokens
-        self.blocks = [GraphedMoEBlock(backend, m, router_w, residual_multiplier, bias=bias)
+        self.from_h = norm_w is not None
+        self.blocks = [GraphedMoEBlock(backend, m, router_w, residual_multiplier, bias=bias,
+                                       norm_w=norm_w, eps=eps)
                        for m in self.sizes]
         self.copy_in = torch.cuda.Stream()
         self.copy_out = torch.cuda.Stream()
@@ -465,7 +503,10 @@ class StreamedMoEBlock:
         self.loaded, self.stepped, self.inputs_free, self.output_free = ev(), ev(), ev(), ev()
 
     def _check(self, x_host, h_host, out_host):
-        if x_host.shape[0] != self.n or h_host.shape[0] != self.n or out_host.shape[0] != self.n:
+        if (x_host is None) != self.from_h:
+            raise ValueError("StreamedMoEBlock: pass x_host exactly when the block has no norm_w")
+        if (x_host is not None and x_host.shape[0] != self.n) or h_host.shape[0] != self.n or \
+                out_host.shape[0] != self.n:
             raise ValueError(f"StreamedMoEBlock: expected {self.n} tokens")
 
     def _enqueue(self, x_host, h_host, out_host, capturing: bool):
@@ -480,7 +521,8 @@ class StreamedMoEBlock:
             with torch.cuda.stream(self.copy_in):
                 if not capturing:
                     self.copy_in.wait_event(self.inputs_free[i])  # last call's step i read blk.x / blk.h
-                blk.x.copy_(x_host[rows], non_blocking=True)
+                if x_host is not None:
+                    blk.x.copy_(x_host[rows], non_blocking=True)
                 blk.h.copy_(h_host[rows], non_blocking=True)
                 self.loaded[i].record(self.copy_in)
             cur.wait_event(self.loaded[i])
@@ -513,7 +555,8 @@ class StreamedMoEBlock:
         with torch.cuda.graph(g):
             self._enqueue(x_host, h_host, out_host, capturing=True)
         self.graph = g
-        self.bound = (x_host.data_ptr(), h_host.data_ptr(), out_host.data_ptr())
+        self.bound = (None if x_host is None else x_host.data_ptr(), h_host.data_ptr(),
+                      out_host.data_ptr())
 
     def __call__(self, x_host, h_host, out_host):
         """Enqueue ``out_host = h_host + moe(x_host) * rm`` on the current
@@ -521,11 +564,23 @@ class StreamedMoEBlock:
         ``out_host`` is complete once the current stream reaches this point."""
         self._check(x_host, h_host, out_host)
         if getattr(self, "graph", None) is not None and self.bound == (
-                x_host.data_ptr(), h_host.data_ptr(), out_host.data_ptr()):
+                None if x_host is None else x_host.data_ptr(), h_host.data_ptr(),
+                out_host.data_ptr()):
             self.graph.replay()
             return out_host
         self._enqueue(x_host, h_host, out_host, capturing=False)
         return out_host
+
+
+def rms_norm(comm: Comm, h, weight, eps: float):
+    """Post-attention RMSNorm on the device (miniep/modeling.py:51-52) with the
+    reference's rounding points in the model dtype."""
+    hh = h.reshape(-1, comm.hidden).contiguous()
+    w = weight.to(device=hh.device, dtype=comm.dtype).contiguous()
+    x = torch.empty_like(hh)
+    check(_lib.lib().mep_rmsnorm(comm._ctx, ptr(hh), ptr(w), float(eps), hh.shape[0], ptr(x),
+                                 _stream()), comm._ctx, "mep_rmsnorm")
+    return x.view_as(h)
 
 
 def router_topk(comm: Comm, x_flat, router_w, bias=None, return_logits: bool = False):

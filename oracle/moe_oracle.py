@@ -125,6 +125,22 @@ def residual_add(h, moe_out, residual_multiplier):
     return h + moe_out * residual_multiplier
 
 
+def rms_norm(x, weight, eps):
+    """``weight * (x * rsqrt(mean(x^2) + eps))`` in the activation dtype
+    (modeling.py:51-52)."""
+    return weight * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps))
+
+
+def moe_block_from_h(h, norm_w, eps, router_w, w_in, w_out, k, residual_multiplier, bias=None,
+                     valid_mask=None):
+    """The MoE half of ``Block.forward`` from the residual stream
+    (modeling.py:192-197): post-attention RMSNorm, router, MoE, residual."""
+    x = rms_norm(h, norm_w, eps)
+    out, idx, gate = moe_block(h, x, router_w, w_in, w_out, k, residual_multiplier, bias,
+                               valid_mask)
+    return out, idx, gate, x
+
+
 def moe_block(h, x, router_w, w_in, w_out, k, residual_multiplier,
               bias=None, valid_mask=None):
     """Router + MoE + residual for one layer (modeling.py:192-197), local experts."""

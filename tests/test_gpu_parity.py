@@ -411,3 +411,62 @@ def test_streamed_block_from_host_matches_unchunked_step():
                                   synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias)
         assert torch.equal(out_host, want.cpu())
     be.comm.check()
+
+
+# ------------------------------------------------------------ block from h
+@pytest.mark.parametrize("shape,dtype", [("a", torch.bfloat16), ("b", torch.bfloat16),
+                                         ("a", torch.float32)])
+def test_rms_norm_matches_reference_formula(shape, dtype):
+    """modeling.py:51-52 in the model dtype: fp32 within 1e-6; bf16 mostly equal
+    to the checker. The fp32 sum of squares runs in another order than torch's,
+    so a row's bf16 mean can round one step apart; its 1/sqrt then moves one
+    step and, through the two rounded products, its outputs up to two."""
+    from miniep_b200.ep import rms_norm
+    sh = synth.SHAPES[shape]
+    n, H = 777, sh["hidden"]
+    h = synth.make_tokens(n, H, seed=21, dtype=dtype)
+    g = torch.Generator().manual_seed(22)
+    w = (1.0 + 0.02 * torch.randn(H, generator=g)).to(dtype)
+    comm = world1_comm(sh["experts"], sh["topk"], H, sh["inter"], n, dtype)
+    x = rms_norm(comm, h.cuda(), w.cuda(), 1e-6).cpu()
+    ref = O.rms_norm(h, w, 1e-6)
+    if dtype == torch.float32:
+        assert (x - ref).abs().max() <= 1e-6 * ref.abs().max()
+    else:
+        two_ulp = ref.float().abs().clamp_min(2.0 ** -20) * 2.0 ** -6
+        assert torch.all((x.float() - ref.float()).abs() <= two_ulp)
+        assert (x == ref).float().mean() > 0.99
+
+
+def test_moe_block_from_h_is_norm_then_block():
+    """The fused entry point equals the norm stage followed by the block, bit
+    for bit, and its graphed and host-streamed forms equal it too."""
+    from miniep_b200 import GraphedMoEBlock, StreamedMoEBlock
+    from miniep_b200.ep import rms_norm
+    sh = synth.SHAPES["a"]
+    n, H = 1000, sh["hidden"]
+    lb = synth.make_layer(H, sh["experts"], sh["inter"], n, seed=23, dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0].cuda()
+    h = synth.make_tokens(n, H, seed=24, dtype=torch.bfloat16).cuda()
+    w = (1.0 + 0.02 * torch.randn(H, generator=torch.Generator().manual_seed(25))).to(
+        torch.bfloat16).cuda()
+    be = world1_backend(lb.w_in, lb.w_out, sh["topk"], n)
+    router, rm = lb.router.cuda(), synth.GRANITE_RESIDUAL_MULTIPLIER
+    out, idx, gate, x = be.moe_block_from_h(h, w, 1e-6, router, rm, bias=bias)
+    x2 = rms_norm(be.comm, h, w, 1e-6)
+    assert torch.equal(x, x2)
+    want, idx2, gate2 = be.moe_block(h, x2, router, rm, bias=bias)
+    assert torch.equal(out, want) and torch.equal(idx, idx2) and torch.equal(gate, gate2)
+    # against the checker: an fp32 block on the same normalised rows and routing
+    ref32 = O.residual_add(h.float().cpu(), _fp32_ref(x.cpu(), idx.cpu(), gate.cpu(), lb.w_in,
+                                                      lb.w_out), rm)
+    assert (out.float().cpu() - ref32).abs().max() <= BF16_ATOL * max(1.0, float(ref32.abs().max()))
+    blk = GraphedMoEBlock(be, n, router, rm, bias=bias, norm_w=w, eps=1e-6)
+    assert torch.equal(blk(h=h).clone(), out)
+    sblk = StreamedMoEBlock(be, n, router, rm, bias=bias, chunks=3, norm_w=w, eps=1e-6)
+    h_host = h.cpu().pin_memory()
+    out_host = torch.empty_like(h_host).pin_memory()
+    sblk(None, h_host, out_host)
+    torch.cuda.synchronize()
+    assert torch.equal(out_host, out.cpu())
+    be.comm.check()
