@@ -68,3 +68,30 @@ def test_dummy_prefill_adds_no_expert_rows(golden):
     shard = Shard([[1, 2, 3]], cfg, 2, "cpu", torch.float32)
     Engine(model).prefill(shard, dummy=True)
     assert seen == [0] * cfg.num_hidden_layers
+
+
+def test_shard_masks_follow_the_reference_engine():
+    """worker.py:55-75: prefill keeps causal keys inside each row's length and
+    expert entries inside it; decode step t sees the row's prompt keys and
+    every decode column written so far; positions continue each row's own."""
+    cfg = ModelConfig(hidden_size=64, intermediate_size=32, num_hidden_layers=1,
+                      num_attention_heads=2, num_key_value_heads=1, num_local_experts=4,
+                      num_experts_per_tok=2, vocab_size=16, rms_norm_eps=1e-6, rope_theta=1e4,
+                      embedding_multiplier=1.0, attention_multiplier=0.125,
+                      residual_multiplier=1.0, logits_scaling=1.0, max_position_embeddings=32)
+    sh = Shard([[1, 2, 3], [4], [5, 6]], cfg, 2, "cpu", torch.float32)
+    assert (sh.T, sh.cap) == (3, 5)
+    assert sh.input.tolist() == [[1, 2, 3], [4, 0, 0], [5, 6, 0]]
+    mask, valid = sh.prefill_masks()
+    assert valid.tolist() == [[True] * 3, [True, False, False], [True, True, False]]
+    # row 1, query 2 (padding): only its valid key 0
+    assert mask[1, 0, 2].tolist() == [True, False, False]
+    assert mask[0, 0].tolist() == [[True, False, False], [True, True, False], [True, True, True]]
+    sh.used = sh.T
+    assert sh.decode_mask()[:, 0, 0].tolist() == [[True, True, True, True],
+                                                   [True, False, False, True],
+                                                   [True, True, False, True]]
+    assert sh.decode_positions().view(-1).tolist() == [3, 1, 2]
+    sh.used, sh.decoded = sh.T + 1, 1
+    assert sh.decode_mask()[1, 0, 0].tolist() == [True, False, False, True, True]
+    assert sh.decode_positions().view(-1).tolist() == [4, 2, 3]
