@@ -21,6 +21,9 @@ the tests that use them never need the reference at run time. What is pinned:
                                known answer plus synthetic skewed count matrices.
 * ``stats_schema.json``       EPStats.snapshot keys and the straggler figures
                                recomputed from the shipped bench results.
+* ``rms_norm.npz``            rms_norm (modeling.py:51-52) in bf16 and fp32 on
+                               shape (a) and (b) rows, the post-attention norm of
+                               the MoE block (modeling.py:192).
 * ``model_tiny.npz``          GraniteMoeModel (modeling.py:148-262) with
                                LocalMoEBackend, driven like the engine's
                                prefill + greedy decode (worker.py:38-138) over a
@@ -265,6 +268,23 @@ def gen_model(out: Path):
                         min_top2_gap=gap)
 
 
+def gen_rms_norm(out: Path):
+    from miniep.modeling import rms_norm
+    res = {}
+    for shape in ("a", "b"):
+        H = synth.SHAPES[shape]["hidden"]
+        g = torch.Generator().manual_seed(31)
+        h = torch.randn(16, H, generator=g)
+        w = 1.0 + 0.02 * torch.randn(H, generator=g)
+        for name, dt in (("bf16", torch.bfloat16), ("fp32", torch.float32)):
+            hd, wd = h.to(dt), w.to(dt)
+            y = rms_norm(hd, wd, 1e-6)
+            res[f"{shape}_{name}_h"] = bf16_bits(hd) if dt == torch.bfloat16 else hd.numpy()
+            res[f"{shape}_{name}_w"] = bf16_bits(wd) if dt == torch.bfloat16 else wd.numpy()
+            res[f"{shape}_{name}_y"] = bf16_bits(y) if dt == torch.bfloat16 else y.numpy()
+    np.savez_compressed(out / "rms_norm.npz", **res)
+
+
 def gen_stats(ref_root: Path, out: Path):
     res = {}
     for name in ("naive", "balanced"):
@@ -303,6 +323,7 @@ def main():
         "balancer": lambda: gen_balancer(ref_root, HERE),
         "stats": lambda: gen_stats(ref_root, HERE),
         "model": lambda: gen_model(HERE),
+        "rms_norm": lambda: gen_rms_norm(HERE),
     }
     for name, fn in steps.items():
         if args.only and name not in args.only.split(","):

@@ -129,3 +129,14 @@ def test_local_equals_world1_ep():
     ep = O.ep_forward([lt.x], [ti], [tg], lt.w_in, lt.w_out, O.naive_owners(1, 8, 1)[0])
     assert torch.allclose(local, ep.outputs[0], rtol=1e-6, atol=1e-7)
     assert ep.recv_tokens[0] == 80
+
+
+def test_rms_norm_matches_reference(golden):
+    """The checker's post-attention RMSNorm is the reference's rms_norm
+    (modeling.py:51-52) bit for bit, bf16 and fp32, shapes (a) and (b)."""
+    g = np.load(golden / "rms_norm.npz")
+    for shape in ("a", "b"):
+        for name in ("bf16", "fp32"):
+            conv = _bf16 if name == "bf16" else torch.from_numpy
+            h, w, y = (conv(g[f"{shape}_{name}_{t}"]) for t in ("h", "w", "y"))
+            assert torch.equal(O.rms_norm(h, w, 1e-6), y), (shape, name)
