@@ -5,19 +5,24 @@ dispatch + grouped SwiGLU experts + combine + residual, modeling.py:192-197).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
-Workload (shape (a)): hidden 1024, 32 experts, top-8,
-intermediate 512, bf16, Zipf(1.2)-skewed router (layer-0 bias), 16384 tokens
-per step in total, split evenly over the ranks (strong scaling), balanced
-replica plan (2 slots per rank) from a naive profiling pass when N > 1.
-Seeded synthetic tensors stand in for the checkpoint and prompts.
+Workload (shape (a) by default): hidden 1024, 32 experts,
+top-8, intermediate 512, bf16, Zipf(1.2)-skewed router (layer-0 bias), 16384
+tokens per step in total, split evenly over the ranks (strong scaling). The
+placement comes from a profiling pass over the same tokens: ``lpt`` (default,
+``plan_lpt``: experts re-placed by load, at most E/N + 2 experts per rank),
+``balanced`` (the reference's replica planner, 2 slots per rank) or
+``naive``. Seeded synthetic tensors stand in for the checkpoint and prompts.
 
 Prints one JSON line (rank 0). `value` is whole-job tokens/s of the device
 step (inputs resident in HBM, L2 flushed between steps, per-step CUDA events,
 max over ranks); `e2e` is the same metric through the public API with the
-step's inputs copied from pinned host memory and its output copied back
-inside the timed region (h is the block's only input). `--impl reference`
-times the CPU checker's restatement of the reference's block (RMSNorm,
-router, LocalMoEBackend, residual) on this host's cores.
+step's input copied from pinned host memory and its output copied back inside
+the timed region. After the timed steps every rank runs one checked step:
+route counts, received rows and sampled output rows against the CPU checker
+(`parity`). A timeline pass records per-stage device stamps on every rank
+(`stages_us`). `--impl reference` times the CPU checker's restatement of the
+reference's block (RMSNorm, router, LocalMoEBackend, residual) on this host's
+cores, on the same tokens.
 """
 from __future__ import annotations
 
@@ -42,26 +47,36 @@ METRIC = "MoE layer tokens/s"
 UNIT = "tokens/s"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_BF16_TFLOPS = 1590.0
+NVLINK_NOMINAL_GBS = 900.0   # per direction per GPU (NVLink 5 through NVSwitch)
+NVLINK_MEASURED_GBS = 770.0  # peer copy per direction, measured on this pool's B200s
 # DRAM bytes (read + write) of the expert FFN stage (both tcgen05 launches) per
 # layer step, from one ncu capture of this bench at N=1 (profiles/
 # ffn_tc_shape_a_16k_dram.txt): keyed by (shape, tokens per step)
 FFN_DRAM_BYTES = {("a", 16384): 325.20e6 + 110.93e6 + 163.11e6 + 215.29e6}
-# norm, router, routing (+ layout), dispatch, gemm1, gemm2, combine (+ data wait and fan-out when N > 1)
-KERNELS_PER_STEP = 7
+NORM_EPS = 1e-6
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--shape", choices=["a", "b"], default="a")
     ap.add_argument("--tokens", type=int, default=16384, help="tokens per step, all ranks")
-    ap.add_argument("--plan", choices=["naive", "balanced"], default="balanced")
-    ap.add_argument("--cpu-sample", type=int, default=2048, help="tokens per CPU sample")
+    ap.add_argument("--plan", choices=["naive", "balanced", "lpt"], default="lpt")
+    ap.add_argument("--slots", type=int, default=2, help="extra expert slots per rank for the plan")
+    ap.add_argument("--cpu-sample", type=int, default=0,
+                    help="tokens per CPU step (0: the whole step, shrunk only if the "
+                         "reference arm would run for more than a few minutes)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="length of the cpu_baseline measurement in the GPU arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--timeline-steps", type=int, default=10,
+                    help="steps of the per-stage timeline pass (0: skip)")
+    ap.add_argument("--parity-rows", type=int, default=256, help="output rows checked per rank")
     ap.add_argument("--e2e-chunks", type=int, default=0,
                     help="pieces per host batch in the e2e leg (0: 4 from 4096 tokens per rank, else 2)")
     ap.add_argument("--force-simt", action="store_true")
@@ -77,18 +92,29 @@ def workload_name(a) -> str:
     return f"moe_layer_shape_{a.shape}_{a.tokens}tok_zipf1.2_{a.plan}"
 
 
+PLAN_NOTES = {
+    "naive": "naive contiguous placement (Placement.naive)",
+    "balanced": "the reference's replica planner (plan_balanced, 2 extra slots per rank)",
+    "lpt": "plan_lpt: experts re-placed by profiled load, longest first, at most E/N + 2 "
+           "experts per rank (same plan JSON)",
+}
+
+
 def config(a, sh) -> dict:
     return {"workload": workload_name(a), "tokens_per_step": a.tokens, "hidden": sh["hidden"],
             "experts": sh["experts"], "topk": sh["topk"], "inter": sh["inter"],
             "block": "post-attention RMSNorm + router + experts + residual from h "
                      "(modeling.py:192-197)",
             "router": "zipf(1.2) bias x2.0, layer 0", "placement": a.plan,
+            "placement_note": PLAN_NOTES[a.plan].replace("2 extra", f"{a.slots} extra")
+                                                .replace("E/N + 2", f"E/N + {a.slots}"),
             "l2": "flushed between timed steps (512 MiB write + 256 MiB read, outside the step events)"}
 
 
 # ------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples of this GPU during the timed region."""
+    """nvidia-smi samples of this GPU over the bench's GPU phase (warm-up,
+    timed graph steps, timeline, e2e)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -103,13 +129,12 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
         except (OSError, ValueError):
             self.proc = None
             return
-        # the timed region starts once sampling runs
         t0 = time.perf_counter()
         while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 5.0:
             time.sleep(0.02)
@@ -146,26 +171,26 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
                 "power_w_max": max(power) if power else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+                "samples": len(sm), "reasons": sorted(reasons),
+                "window": "every 100 ms over the GPU phase (warm-up, timed steps, timeline, e2e)"}
 
 
 # --------------------------------------------------------------- CPU legs
-def cpu_sample_inputs(sh, n_tokens, seed=0):
-    from miniep_b200 import synth
-    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n_tokens, seed=seed,
-                          dtype=torch.bfloat16)
-    bias = synth.zipf_router_bias(1, sh["experts"])[0]
-    h = synth.make_tokens(n_tokens, sh["hidden"], seed=seed + 7, dtype=torch.bfloat16)
-    return lb, bias, h
-
-
-NORM_EPS = 1e-6
-
-
 def norm_weight(hidden: int, device=None):
     """Synthetic post-attention RMSNorm weight: 1 + N(0, 1) * 0.02 (seed 8)."""
     g = torch.Generator().manual_seed(8)
     return (1.0 + 0.02 * torch.randn(hidden, generator=g)).to(torch.bfloat16).to(device)
+
+
+def cpu_inputs(sh, n_tokens):
+    """The bench's own tokens and weights on the host (drawn on the CPU with the
+    same seeds as the GPU arm's CPU copies)."""
+    from miniep_b200 import synth
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], 1, seed=0,
+                          dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0]
+    h = synth.make_tokens(n_tokens, sh["hidden"], seed=7, dtype=torch.bfloat16)
+    return lb, bias, h
 
 
 def cpu_step(oracle, lb, bias, h, k):
@@ -176,25 +201,26 @@ def cpu_step(oracle, lb, bias, h, k):
     return out
 
 
-def cpu_baseline(sh, sample_tokens, min_seconds=10.0, max_reps=2000) -> dict:
-    """The CPU checker's restatement of the reference path (router +
-    LocalMoEBackend + residual) on this host's cores, on a bounded sample."""
+def cpu_baseline(sh, tokens, seconds) -> dict:
+    """The CPU checker's restatement of the reference path (RMSNorm, router,
+    LocalMoEBackend, residual) on this host's cores, on the bench's own
+    token batch, repeated for about `seconds`."""
     from oracle import moe_oracle
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    lb, bias, h = cpu_sample_inputs(sh, sample_tokens)
+    lb, bias, h = cpu_inputs(sh, tokens)
     cpu_step(moe_oracle, lb, bias, h, sh["topk"])  # warm-up
     reps, t0 = 0, time.perf_counter()
-    while reps < max_reps:
+    while True:
         cpu_step(moe_oracle, lb, bias, h, sh["topk"])
         reps += 1
-        if time.perf_counter() - t0 >= min_seconds:
+        if time.perf_counter() - t0 >= seconds:
             break
     dt = time.perf_counter() - t0
-    return {"value": reps * sample_tokens / dt, "unit": UNIT, "cores": torch.get_num_threads(),
+    return {"value": reps * tokens / dt, "unit": UNIT, "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"{reps} x {sample_tokens} tokens of the same workload (bf16, shape, "
-                      f"Zipf router) through oracle.moe_block_from_h, {dt:.1f} s"}
+            "sample": f"{reps} x the full {tokens}-token step (bf16, same shape, Zipf router) "
+                      f"through oracle.moe_block_from_h in one process, {dt:.1f} s"}
 
 
 def run_reference(a):
@@ -207,8 +233,15 @@ def run_reference(a):
     sh = synth.SHAPES[a.shape]
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    sample = min(a.cpu_sample, a.tokens)
-    lb, bias, h = cpu_sample_inputs(sh, sample)
+    sample = min(a.cpu_sample or a.tokens, a.tokens)
+    lb, bias, h = cpu_inputs(sh, sample)
+    t0 = time.perf_counter()
+    cpu_step(moe_oracle, lb, bias, h, sh["topk"])
+    t_one = time.perf_counter() - t0
+    if not a.cpu_sample and (a.steps + a.warmup) * t_one > 150.0:
+        # keep the whole run within a few minutes: a bounded sample per step
+        sample = max(256, int(sample * 150.0 / ((a.steps + a.warmup) * t_one)) // 256 * 256)
+        h = h[:sample].contiguous()
     for _ in range(a.warmup):
         cpu_step(moe_oracle, lb, bias, h, sh["topk"])
     t0 = time.perf_counter()
@@ -221,21 +254,57 @@ def run_reference(a):
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": dt / a.steps * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": config(a, sh),
+        "same_config": sample == a.tokens,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{sample} tokens per step through oracle.moe_block_from_h "
-                                   f"(router + LocalMoEBackend + residual restated in torch CPU)"},
+                         "sample": f"{sample} of the step's {a.tokens} tokens per step through "
+                                   f"oracle.moe_block_from_h (router + LocalMoEBackend + residual "
+                                   f"restated in torch CPU ops, one process on all host threads)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # --------------------------------------------------------------- GPU leg
+def make_plan(kind, counts, world, slots):
+    from miniep_b200 import Placement, plan_balanced, plan_lpt
+    E = counts.numel()
+    if world == 1 or kind == "naive":
+        return Placement.naive(1, E, world), None
+    if kind == "balanced":
+        return plan_balanced(counts.view(1, E).cpu(), world, slots_per_rank=slots)
+    return plan_lpt(counts.view(1, E).cpu(), world, slots_per_rank=slots)
+
+
+def layer_roofline(sh, tokens, world, ms_step, remote_entries, peak_tflops):
+    """The north-star layer roofline: the slower of the expert FLOPs at the
+    tensor peak and the dispatch + combine bytes at NVLink bandwidth.
+    remote_entries: per rank (entries it sends to other ranks, entries it
+    receives from other ranks), one row each way per phase (no dedup)."""
+    H, E, k, I = sh["hidden"], sh["experts"], sh["topk"], sh["inter"]
+    f_tok = 6.0 * k * H * I + 2.0 * H * E
+    t_tc = tokens * f_tok / world / (peak_tflops * 1e12) * 1e6
+    row = H * 2.0
+    # per direction per phase: the busiest rank's remote rows; dispatch sends
+    # what combine later receives, so each phase moves max(sent, received)
+    nv_bytes = max((2.0 * max(s, r) * row for s, r in remote_entries), default=0.0)
+    t_nv = {bw: nv_bytes / (bw * 1e9) * 1e6 for bw in (NVLINK_NOMINAL_GBS, NVLINK_MEASURED_GBS)}
+    roof_us = max(t_tc, t_nv[NVLINK_NOMINAL_GBS])
+    return {"t_tc_us": t_tc, "t_nv_us": t_nv[NVLINK_NOMINAL_GBS],
+            "t_nv_us_at_measured_770": t_nv[NVLINK_MEASURED_GBS],
+            "nvlink_bytes_max_rank": nv_bytes, "roofline_us": roof_us,
+            "roofline_tokens_per_s": tokens / (roof_us / 1e6),
+            "frac": roof_us / (ms_step * 1e3),
+            "assumptions": f"T_tc: {f_tok:.0f} FLOP/token at the measured burst bf16 peak "
+                           f"{peak_tflops} TFLOP/s; T_nv: per-entry rows (no dedup), both "
+                           f"phases, at {NVLINK_NOMINAL_GBS:.0f} GB/s per direction (nominal "
+                           "NVLink 5)"}
+
+
 def main_b200(a):
     import torch.distributed as dist
-    from miniep_b200 import (Comm, EPMoEBackend, EPStats, GraphedMoEBlock, Placement,
-                             StreamedMoEBlock, _lib, plan_balanced, report, straggler_overhead,
-                             synth)
+    from miniep_b200 import (Comm, EPMoEBackend, EPStats, GraphedMoEBlock, StreamedMoEBlock,
+                             _lib, report, straggler_overhead, synth)
     from miniep_b200.ep import rms_norm, router_topk
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -245,16 +314,19 @@ def main_b200(a):
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    clocks = ClockSampler(local)
+    clocks.start()
     sh = synth.SHAPES[a.shape]
     H, E, k, I = sh["hidden"], sh["experts"], sh["topk"], sh["inter"]
     start, stop = synth.split_tokens(a.tokens, world, rank)
     n = stop - start
-    # same weights on every rank (same seed), each rank its own token shard
-    lt = synth.make_layer(H, E, I, a.tokens, seed=0, dtype=torch.bfloat16, device=dev)
+    # same weights on every rank (same seed), each rank its own token shard;
+    # drawn on the host, so they are the reference arm's tensors too
+    lt_cpu = synth.make_layer(H, E, I, 1, seed=0, dtype=torch.bfloat16)
+    lt = synth.LayerTensors(lt_cpu.router.to(dev), lt_cpu.w_in.to(dev), lt_cpu.w_out.to(dev), None)
     bias = synth.zipf_router_bias(1, E)[0].to(dev)
-    h = synth.make_tokens(a.tokens, H, seed=7, dtype=torch.bfloat16, device=dev)[start:stop].contiguous()
+    h = synth.make_tokens(a.tokens, H, seed=7, dtype=torch.bfloat16)[start:stop].to(dev)
     nw = norm_weight(H, dev)
     rm = synth.GRANITE_RESIDUAL_MULTIPLIER
 
@@ -262,20 +334,22 @@ def main_b200(a):
                 dtype=torch.bfloat16, device=local, timeout_ms=20000)
     if a.force_simt:
         comm.set_option("force_simt", 1)
-    placement = Placement.naive(1, E, world)
-    counts = None
-    if world > 1 and a.plan == "balanced":
-        comm.install(placement)
-        idx, _ = router_topk(comm, rms_norm(comm, h, nw, NORM_EPS), lt.router, bias)
-        counts = torch.bincount(idx.reshape(-1), minlength=E).to(torch.int64)
+    from miniep_b200 import Placement
+    comm.install(Placement.naive(1, E, world))
+    # profiling pass: the global per-expert load of these tokens
+    idx0, _ = router_topk(comm, rms_norm(comm, h, nw, NORM_EPS), lt.router, bias)
+    counts = torch.bincount(idx0.reshape(-1), minlength=E).to(torch.int64)
+    if world > 1:
         dist.all_reduce(counts)
-        placement, _ = plan_balanced(counts.view(1, E).cpu(), world, slots_per_rank=2)
+    placement, plan_report = make_plan(a.plan, counts, world, a.slots)
     comm.install(placement)
     mine = placement.experts_of_rank(rank)[0]
     w_in, w_out = lt.w_in[mine].contiguous(), lt.w_out[mine].contiguous()
-    lt_router = lt.router.contiguous()
-    del lt
-    stats = EPStats(1, E)  # device counters; the report covers the timed graph steps only
+    router_w = lt.router.contiguous()
+    w_in_all, w_out_all = ((lt_cpu.w_in, lt_cpu.w_out) if rank == 0 and not a.no_parity
+                           else (None, None))
+    del lt, lt_cpu
+    stats = EPStats(1, E)
     be = EPMoEBackend(0, comm, placement, mine, w_in, w_out, stats)
 
     L, ctx = _lib.lib(), comm._ctx
@@ -297,7 +371,7 @@ def main_b200(a):
     def eager_step(st, ev_ffn=None):
         # mep_moe_block_from_h's sequence, with events around the expert FFN stage
         _lib.check(L.mep_rmsnorm(ctx, P(h), P(nw), NORM_EPS, n, P(x), st), ctx)
-        _lib.check(L.mep_router_topk(ctx, P(x), P(lt_router), P(bias), n, P(idx), P(gate),
+        _lib.check(L.mep_router_topk(ctx, P(x), P(router_w), P(bias), n, P(idx), P(gate),
                                      None, st), ctx)
         _lib.check(L.mep_route(ctx, 0, P(idx), None, n, len(mine), st), ctx)
         _lib.check(L.mep_dispatch(ctx, P(x), P(idx), n, st), ctx)
@@ -338,7 +412,7 @@ def main_b200(a):
     comm.check()
 
     # 1) eager stages: FFN-stage time for the roofline, and the eager step time
-    n_eager = max(10, a.steps // 4)
+    n_eager = max(10, min(a.steps // 4, 50))
     ffn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_eager)]
     eager_ms = timed(lambda i: eager_step(st, ffn[i]), n_eager)
@@ -347,34 +421,59 @@ def main_b200(a):
     comm.check()
 
     # 2) the step as one CUDA graph (GraphedMoEBlock): the reported value
-    blk = GraphedMoEBlock(be, n, lt_router, rm, bias=bias, norm_w=nw, eps=NORM_EPS)
+    blk = GraphedMoEBlock(be, n, router_w, rm, bias=bias, norm_w=nw, eps=NORM_EPS)
     blk.h.copy_(h)
     for _ in range(a.warmup):
         blk()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
     _lib.check(L.mep_reset_stats(ctx, st), ctx)
-    clocks.start()
     wall0 = time.perf_counter()
     step_ms = timed(lambda i: blk(), a.steps)
     wall = time.perf_counter() - wall0
     comm.check()
     t_step = torch.tensor([sum(step_ms) / a.steps, sum(ffn_ms) / n_eager,
                            sum(eager_ms) / n_eager], device=dev, dtype=torch.float64)
-    rows_t = torch.tensor([recv_rows], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t_step, op=dist.ReduceOp.MAX)
     ms_step, ms_ffn, ms_eager = t_step.tolist()
     snap = stats.snapshot()  # route counts and received entries of the timed steps
+    timed_recv = snap["recv_tokens"] / a.steps
 
-    # 3) e2e: the public graphed API with host buffers, copies inside the timed region
+    # 3) timeline: per-stage device stamps of the graphed step on every rank
+    stages = None
+    if a.timeline_steps > 0:
+        comm.set_option("timeline", 1)
+        tblk = GraphedMoEBlock(be, n, router_w, rm, bias=bias, norm_w=nw, eps=NORM_EPS)
+        comm.set_option("timeline", 0)
+        tblk.h.copy_(h)
+        comm.read_timeline()  # clears the construction step's stamps
+        recs = []
+        if world > 1:
+            dist.barrier()
+        for _ in range(a.timeline_steps):
+            flush_l2()
+            if world > 1:
+                comm.barrier()
+            tblk()
+            recs.append(comm.read_timeline())
+        comm.check()
+        del tblk
+        stages = {}
+        for key in recs[0]:
+            vals = [r[key] for r in recs if key in r]
+            if isinstance(vals[0], tuple):
+                stages[key] = [round(statistics.median(v[0] for v in vals), 1),
+                               round(statistics.median(v[1] for v in vals), 1)]
+            else:
+                stages[key] = round(statistics.median(vals), 1)
+
+    # 4) e2e: the public graphed API with host buffers, copies inside the timed region
     e2e = None
     if not a.no_e2e:
         h_host = h.cpu().pin_memory()
         out_host = torch.empty_like(h_host).pin_memory()
-
         chunks = a.e2e_chunks or (4 if n >= 4096 else 2)
-        sblk = StreamedMoEBlock(be, n, lt_router, rm, bias=bias, chunks=chunks, norm_w=nw,
+        sblk = StreamedMoEBlock(be, n, router_w, rm, bias=bias, chunks=chunks, norm_w=nw,
                                 eps=NORM_EPS)
         graphed = a.e2e_graph == "on"
         if graphed:
@@ -406,22 +505,41 @@ def main_b200(a):
                        + (", one CUDA graph per step" if graphed else
                           ", eager (consecutive steps overlap)")}
         comm.check()
+        del sblk
     clk = clocks.stop()
 
-    # per-rank received rows and expert-stage time: the straggler figures
-    per_rank = torch.tensor([[float(recv_rows), sum(ffn_ms) / n_eager]], device=dev,
-                            dtype=torch.float64)
+    # 5) one checked step: round-robin state reset, so the checker can follow it
+    parity_in = None
+    if not a.no_parity:
+        be.placement.reset_rr()
+        _lib.check(L.mep_reset_stats(ctx, st), ctx)
+        p_out, p_idx, p_gate, p_x = be.moe_block_from_h(h, nw, NORM_EPS, router_w, rm, bias=bias)
+        comm.check()
+        psnap = stats.snapshot()
+        g = torch.Generator().manual_seed(1000 + rank)
+        rows = torch.randperm(n, generator=g)[:min(a.parity_rows, n)].sort().values
+        parity_in = {"rank": rank, "idx": p_idx.cpu(), "recv": psnap["recv_tokens"],
+                     "route_counts": psnap["route_counts"][0], "rows": rows,
+                     "h": h[rows.to(dev)].cpu(), "x": p_x[rows.to(dev)].cpu(),
+                     "gate": p_gate[rows.to(dev)].cpu(), "out": p_out[rows.to(dev)].cpu()}
+        del p_out, p_idx, p_gate, p_x
+
+    # gather the per-rank figures on rank 0
+    per_rank = {"rank": rank, "recv_rows": recv_rows, "timed_recv_per_step": timed_recv,
+                "ffn_ms": sum(ffn_ms) / n_eager, "step_ms": sum(step_ms) / a.steps,
+                "stages_us": stages, "parity_in": parity_in}
     if world > 1:
-        parts = [torch.zeros_like(per_rank) for _ in range(world)]
-        dist.all_gather(parts, per_rank)
-        per_rank = torch.cat(parts)
-        dist.all_reduce(rows_t)
-    total_rows = rows_t.item()
+        got = [None] * world if rank == 0 else None
+        dist.gather_object(per_rank, got, dst=0)
+    else:
+        got = [per_rank]
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        cpu = cpu_baseline(sh, a.cpu_sample)
+        cpu = cpu_baseline(sh, a.tokens, a.cpu_seconds)
 
     if rank == 0:
+        got.sort(key=lambda r: r["rank"])
         peaks = json.loads(PEAKS_FILE.read_text()) if PEAKS_FILE.exists() else {}
         # burst figure: the clock samples show the step running at full SM clock,
         # not at the power-capped clock of the sustained figure
@@ -430,10 +548,12 @@ def main_b200(a):
         if peak is None:
             peak, peak_src = FALLBACK_BF16_TFLOPS, "fallback"
         flops_rank0 = recv_rows * 6.0 * H * I  # algorithmic FLOPs of this rank's FFN launch
-        # GEMM1 reads rows (H) and writes act (I); GEMM2 reads act (I), writes rows (H);
-        # plus this rank's expert weights once per launch
         n_local_w_bytes = len(mine) * 3.0 * H * I * 2
         achieved = flops_rank0 / (sum(ffn_ms) / n_eager / 1e3) / 1e12
+        parity, remote = None, None
+        if parity_in is not None:
+            parity, remote = check_parity(got, placement, w_in_all, w_out_all, router_w.cpu(),
+                                          bias.cpu(), sh, rm, world)
         line = {
             "metric": METRIC, "value": a.tokens / (ms_step / 1e3), "unit": UNIT,
             "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step,
@@ -453,25 +573,37 @@ def main_b200(a):
             "ffn_ms_per_step_max_rank": ms_ffn,
             "eager": {"value": a.tokens / (ms_eager / 1e3), "ms_per_step": ms_eager,
                       "note": "same kernels launched one by one from Python"},
-            "layer_roofline_frac": (a.tokens * (6.0 * k * H * I + 2.0 * H * E) / world
-                                    / (ms_step / 1e3) / 1e12) / peak,
-            "recv_rows_total": total_rows,
+            "recv_rows_per_rank": [r["recv_rows"] for r in got],
             "wall_s_timed_region": wall,
-            "gpu_launches": (KERNELS_PER_STEP + 2 * (world > 1)) * a.steps,
+            # per step: norm, router, routing, dispatch, gemm1, gemm2, combine
+            # (+ data wait and fan-out, and the step-start rank barrier, when N > 1)
+            "gpu_launches": (7 + 3 * (world > 1)) * a.steps,
             "clocks": clk,
         }
+        if remote is not None:
+            line["layer_roofline"] = layer_roofline(sh, a.tokens, world, ms_step, remote, peak)
+        if stages is not None:
+            line["stages_us"] = {str(r["rank"]): r["stages_us"] for r in got}
+            line["stages_note"] = ("median device stamps (us) of the graphed step, after the "
+                                   "step-start rank barrier (N = 1: after the first stamp); "
+                                   "[start, end] per stage, single values are wait ends")
+            if remote is not None:
+                line["nvlink"] = nvlink_rates(got, remote, H)
+        if parity is not None:
+            line["parity"] = parity
         if world > 1:
-            loads = per_rank[:, 0].cpu().view(world, 1)
-            t_ffn = per_rank[:, 1].cpu()
+            loads = [[r["timed_recv_per_step"]] for r in got]
+            t_ffn = torch.tensor([r["ffn_ms"] for r in got])
             strag = {"formula": "sum_l max_r recv / sum_l mean_r recv - 1 (1 layer)",
-                     "plan": a.plan,
+                     "plan": a.plan, "slots_per_rank": a.slots,
                      "load_pct": 100.0 * straggler_overhead(loads),
                      "ffn_time_pct": 100.0 * float(t_ffn.max() / t_ffn.mean() - 1.0),
-                     "recv_rows_per_rank": loads.view(-1).tolist()}
-            if counts is not None:  # what the naive placement would have given
-                per = E // world
-                naive = counts.cpu().view(world, per).sum(dim=1).view(world, 1)
-                strag["naive_load_pct"] = 100.0 * straggler_overhead(naive)
+                     "recv_rows_per_rank_per_step": [l[0] for l in loads]}
+            if plan_report is not None:
+                strag["planner_predicted_pct"] = 100.0 * (
+                    plan_report["layers"][0]["imbalance_after"] - 1.0)
+                strag["replicas"] = plan_report["replicas_total"]
+            strag.update(planner_alternatives(counts, world))
             line["straggler"] = strag
         if e2e:
             line["e2e"] = e2e
@@ -484,9 +616,9 @@ def main_b200(a):
         my_ffn, my_step = sum(ffn_ms) / n_eager, sum(step_ms) / a.steps
         snap.update(compute_time=my_ffn * a.steps / 1e3,
                     a2a_time=max(my_step - my_ffn, 0.0) * a.steps / 1e3, steps=a.steps)
-        got = report.gather_payloads(report.rank_payload(rank, n * a.steps, snap))
+        rep_in = report.gather_payloads(report.rank_payload(rank, n * a.steps, snap))
         if rank == 0:
-            rep = report.bench_report(got, plan=a.plan, iters=a.steps, wall_time=wall,
+            rep = report.bench_report(rep_in, plan=a.plan, iters=a.steps, wall_time=wall,
                                       iter_times=[t / 1e3 for t in step_ms])
             report.write_bench_report(a.report, rep)
             for line_ in report.summary_lines(rep):
@@ -496,6 +628,116 @@ def main_b200(a):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def planner_alternatives(counts, world) -> dict:
+    """What the other planners predict for the same counts (max/mean - 1, %),
+    with the extra expert slots per rank each needs (the memory cost)."""
+    from miniep_b200 import plan_balanced, plan_lpt
+    from miniep_b200.balancer import rank_loads
+    E = counts.numel()
+    c = counts.view(1, E).cpu()
+    loads = [float(v) for v in c[0]]
+    mean = sum(loads) / world
+    naive = rank_loads(loads, [[e // (E // world)] for e in range(E)], world)
+    out = {"naive_predicted_pct": 100.0 * (max(naive) / mean - 1.0)}
+    for slots in (2, 4, 8):
+        for name, fn in (("balanced", plan_balanced), ("lpt", plan_lpt)):
+            _, rep = fn(c, world, slots_per_rank=slots)
+            out[f"{name}_slots{slots}_predicted_pct"] = round(
+                100.0 * (rep["layers"][0]["imbalance_after"] - 1.0), 2)
+    return out
+
+
+def check_parity(got, placement, w_in_all, w_out_all, router_w, bias, sh, rm, world):
+    """Rank 0: the checked step of every rank against the CPU checker.
+
+    * counts_exact: each rank's device route counts equal the histogram of
+      its own top-k ids (route_counts, ep.py:216-217);
+    * recv_rows_exact: each rank's received rows equal what the checker's
+      replica round-robin (dest_ranks, ep.py:76-96, state reset to zero)
+      sends it from all ranks' ids;
+    * output rows: sampled rows of h_out against the checker's expert math on
+      the device's own routing (run_experts + slot-order sum + residual,
+      modeling.py:83-128, :197) in fp32 (tolerance 2e-2 max-abs, scaled by
+      max(1, |ref|)) and in bf16 with the reference's rounding points;
+    * router: the checker's top-k on the same normalised rows, rows with an
+      exact tie in the top-(k+1) logits excluded, and the rows whose choice
+      differs only because a logit rounded one step apart counted apart."""
+    import numpy as np
+    from oracle import moe_oracle as O
+    k, E = sh["topk"], sh["experts"]
+    table, n_rep = O.build_table(placement.owners[0])
+    counts_ok, recv_expect = True, np.zeros(world, dtype=np.int64)
+    remote_in = np.zeros(world, dtype=np.int64)
+    sent = []
+    for r in got:
+        pin = r["parity_in"]
+        ids = pin["idx"].reshape(-1).numpy()
+        hist = np.bincount(ids, minlength=E)
+        counts_ok &= hist.tolist() == list(pin["route_counts"])
+        dest = O.dest_ranks(table, n_rep, np.zeros(E, dtype=np.int64), ids)
+        per_dest = np.bincount(dest, minlength=world)
+        recv_expect += per_dest
+        sent.append(int(per_dest.sum() - per_dest[r["rank"]]))
+        remote_in += per_dest
+        remote_in[r["rank"]] -= per_dest[r["rank"]]
+    recv_got = [int(r["parity_in"]["recv"]) for r in got]
+    # per rank: (entries sent to other ranks, entries received from other ranks)
+    remote = [(sent[i], int(remote_in[i])) for i in range(world)]
+    x = torch.cat([r["parity_in"]["x"] for r in got])
+    hh = torch.cat([r["parity_in"]["h"] for r in got])
+    out = torch.cat([r["parity_in"]["out"] for r in got])
+    gate = torch.cat([r["parity_in"]["gate"] for r in got])
+    idx = torch.cat([r["parity_in"]["idx"][r["parity_in"]["rows"]] for r in got])
+    moe32 = O.local_moe(x.float(), idx, gate.float(), w_in_all.float().cpu(),
+                        w_out_all.float().cpu())
+    ref32 = O.residual_add(hh.float(), moe32, rm)
+    err32 = (out.float() - ref32).abs()
+    tol = 2e-2 * max(1.0, float(ref32.abs().max()))
+    moe16 = O.local_moe(x, idx, gate, w_in_all.cpu(), w_out_all.cpu())
+    ref16 = O.residual_add(hh, moe16, rm)
+    d16 = (out.float() - ref16.float()).abs()
+    logits = O.router_logits(x, router_w, bias)
+    ties = O.boundary_ties(logits, k)
+    ref_idx = O.topk_lowest_index(logits, k)
+    same = (ref_idx.sort(dim=1).values == idx.sort(dim=1).values).all(dim=1)
+    return {"counts_exact": bool(counts_ok),
+            "recv_rows_exact": [int(v) for v in recv_expect] == recv_got,
+            "recv_rows": recv_got,
+            "rows": int(out.shape[0]),
+            "max_abs": float(err32.max()), "tol": tol, "ok": bool(float(err32.max()) <= tol),
+            "max_abs_vs_bf16_ref": float(d16.max()),
+            "bitexact_frac_vs_bf16_ref": float((d16 == 0).float().mean()),
+            "router_rows_checked": int((~ties).sum()),
+            "router_mismatch_rows": int((~same & ~ties).sum()),
+            "router_exact_tie_rows": int(ties.sum()),
+            "checker": "oracle/moe_oracle.py (dest_ranks, local_moe, residual_add, router_logits)",
+            }, remote
+
+
+def nvlink_rates(got, remote, H) -> dict:
+    """Per rank: bytes its kernels push over NVLink and the stage time they
+    took (from the timeline): dispatch sends each token row once per remote
+    destination rank it needs (deduplicated rows are fewer than the remote
+    entries; the entry count is the upper bound used here), GEMM2 returns one
+    row per remote entry it computed, overlapped with its tensor-core work."""
+    out = {}
+    for r in got:
+        st = r["stages_us"] or {}
+        sent, recv_remote = remote[r["rank"]]
+        row = 2.0 * H
+        d = st.get("dispatch")
+        g2 = st.get("gemm2")
+        out[str(r["rank"])] = {
+            "dispatch_remote_entries": sent,
+            "dispatch_us": None if not d else round(d[1] - d[0], 1),
+            "gemm2_return_rows": recv_remote,
+            "gemm2_us": None if not g2 else round(g2[1] - g2[0], 1),
+            "return_gbs_lower_bound": None if not g2 else round(
+                recv_remote * row / ((g2[1] - g2[0]) * 1e-6) / 1e9, 1),
+        }
+    return out
 
 
 def main():

@@ -203,9 +203,38 @@ int mep_check(mep_ctx* ctx);
 
 /*
  * Options: "force_simt" (1 = CUDA-core expert GEMMs for bf16 too),
- * "timeout_ms" (bound on every cross-rank wait, default 10000).
+ * "timeout_ms" (bound on every cross-rank wait, default 10000),
+ * "tc_single_cta" (1 = one CTA per 128-row expert tile instead of CTA pairs),
+ * "timeline" (1 = kernels stamp the step timeline read by mep_read_timeline;
+ * launches enqueued or captured while it is 0 stamp nothing).
  */
 int mep_set_option(mep_ctx* ctx, const char* name, int64_t value);
+
+/*
+ * Step timeline (profiling aid, no counterpart in the reference): with the
+ * "timeline" option set, each stage of a layer step records %globaltimer
+ * stamps in nanoseconds: slot S = the stage's start (its first CTA), S + 1 =
+ * its end (the last of its CTAs to finish); the single-point slots mark when
+ * a wait ended. mep_read_timeline copies MEP_TL_SLOTS stamps to `out` (host),
+ * synchronises `stream`, then zeroes the stamps. A stage that did not run
+ * reads 0. Stamps of different GPUs come from different clocks; compare each
+ * rank's stamps with its own MEP_TL_BARRIER_END.
+ */
+#define MEP_TL_BARRIER_END 0  /* mep_barrier: every rank arrived */
+#define MEP_TL_NORM 1         /* k_rmsnorm start, end */
+#define MEP_TL_ROUTER 3       /* router start, end */
+#define MEP_TL_ROUTE 5        /* routing start, end */
+#define MEP_TL_COUNTS_SENT 7  /* this rank's counts stored at every rank */
+#define MEP_TL_LAYOUT 8       /* every rank's counts in, receive layout written */
+#define MEP_TL_DISPATCH 9     /* dispatch start, end */
+#define MEP_TL_DATA_IN 11     /* every rank's rows for this rank landed */
+#define MEP_TL_FANOUT 12      /* landing-row fan-out start, end */
+#define MEP_TL_GEMM1 14       /* expert GEMM1 + SwiGLU start, end */
+#define MEP_TL_GEMM2 16       /* expert GEMM2 + return stores start, end */
+#define MEP_TL_RESULTS_IN 18  /* every owner's results for this rank landed */
+#define MEP_TL_COMBINE 19     /* combine start, end */
+#define MEP_TL_SLOTS 24
+int mep_read_timeline(mep_ctx* ctx, uint64_t* out, void* stream);
 
 /*
  * Rank barrier on the device: this rank's kernel raises its flag on every
@@ -235,14 +264,22 @@ int mep_debug_wait(mep_ctx* ctx, uint32_t target, int64_t timeout_ms, void* stre
  *   table (host, E x rmax int64) / n_rep (host, E int64): one layer's
  *     placement, as for mep_set_placement; world: ranks in the placement;
  *   rr (device, E int64): round-robin state of that layer, updated in place
- *     (zero it to reset, like Placement.reset_rr);
+ *     (zero it to reset, like Placement.reset_rr); any value is accepted, the
+ *     replica being (rr + occurrence) mod n_rep taken non-negative, as
+ *     Python's % gives it;
  *   expert_ids / dest_out (device, m int64), m <= 65536.
+ * An id outside [0, E) gets destination -1 and does not advance the
+ * round-robin state, as in mep_dest_ranks; but where mep_dest_ranks also
+ * records a device error for mep_check, this entry point has no context to
+ * record it in and reports nothing, so validate ids that can be out of range.
  * Its intermediate buffers live in one fixed array of about 650 KiB that
  * every GPU loading this library keeps until the process exits. All calls
  * share that array: calls whose kernels can overlap on one GPU race, so the
- * caller must serialise them. The first call on each device looks up the
- * array's device address; make it before any stream capture. Larger calls
- * fail with MEP_ERR_INVALID; messages come from mep_last_error(NULL).
+ * caller must serialise them. Every call copies the placement table from
+ * host stack memory (pageable) with cudaMemcpyAsync, and the first call on
+ * each device also looks up the array's device address, so no call may be
+ * made while its stream is being captured. Larger calls fail with
+ * MEP_ERR_INVALID; messages come from mep_last_error(NULL).
  */
 int mep_dest_ranks_noalloc(int num_experts, int world, const int64_t* table,
                            const int64_t* n_rep, int rmax, int64_t* rr,

@@ -38,6 +38,8 @@ struct mep_ctx {
   int* err_host = nullptr;
   int* err_dev = nullptr;
   uint32_t* seq = nullptr;  // device: sequence number of the current layer step
+  uint64_t* tl = nullptr;   // device: step timeline stamps (MEP_TL_SLOTS)
+  int tl_on = 0;            // pass tl to the kernels (option "timeline")
   unsigned long long timeout_ns = 10ull * 1000 * 1000 * 1000;
   int force_simt = 0;
   int tc_single_cta = 0;
@@ -84,6 +86,8 @@ void build_peers(mep_ctx* c) {
 }
 
 WaitCfg wait_cfg(const mep_ctx* c) { return WaitCfg{c->err_dev, c->timeout_ns}; }
+
+uint64_t* tl_of(const mep_ctx* c) { return c->tl_on ? c->tl : nullptr; }
 
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
@@ -212,6 +216,7 @@ int mep_ctx_create(int rank, int world, int device, int num_layers, int num_expe
       {reinterpret_cast<void**>(&c->recv_per_layer), (size_t)num_layers * 8},
       {reinterpret_cast<void**>(&c->done_ctr), 4 * sizeof(unsigned int)},
       {reinterpret_cast<void**>(&c->seq), 2 * sizeof(uint32_t)},  // [0] layer step, [1] barrier
+      {reinterpret_cast<void**>(&c->tl), (size_t)kTlSlots * sizeof(uint64_t)},
   };
   for (auto& a : allocs) {
     e = cudaMalloc(a.p, a.bytes);
@@ -241,7 +246,7 @@ int mep_ctx_destroy(mep_ctx* c) {
     if (c->peer_open[r] && c->peer_base[r]) cudaIpcCloseMemHandle(c->peer_base[r]);
   void* ptrs[] = {c->sym,      c->act,    c->recv_x,     c->chunk_hist,   c->ent_dest,     c->ent_grp,
                   c->my_counts, c->layout, c->owners,     c->nrep,         c->rr,
-                  c->route_counts, c->recv_per_layer, c->done_ctr, c->seq};
+                  c->route_counts, c->recv_per_layer, c->done_ctr, c->seq, c->tl};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (c->err_host) cudaFreeHost(c->err_host);
@@ -342,7 +347,7 @@ int mep_router_topk(mep_ctx* c, const void* x, const void* router_w, const float
     return fail(c, MEP_ERR_INVALID, "NULL argument");
   if (int rc = use_device(c)) return rc;
   launch_router(c->dtype, x, router_w, bias, n, c->H, c->E, c->k, topk_idx_out, topk_gate_out,
-                logits_out, c->num_sms, c->err_dev, as_stream(stream));
+                logits_out, c->num_sms, c->err_dev, tl_of(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   return MEP_OK;
 }
@@ -367,7 +372,7 @@ int mep_route(mep_ctx* c, int layer, const int64_t* topk_idx, const uint8_t* val
                c->my_counts, c->peers, c->seq, c->done_ctr + 2, c->num_sms,
                reinterpret_cast<const int32_t*>(c->sym + c->off_cnt),
                reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->recv_per_layer + layer,
-               c->cap_rows, c->layout, wait_cfg(c), as_stream(stream));
+               c->cap_rows, c->layout, wait_cfg(c), tl_of(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   c->stage = 1;
   return MEP_OK;
@@ -384,16 +389,17 @@ int mep_dispatch(mep_ctx* c, const void* x, const int64_t* topk_idx, int64_t n, 
   // the receive layout was computed by mep_route's kernel
   launch_dispatch(c->dtype, n, c->k, c->H, c->world, c->rank, c->max_tokens,
                   x, topk_idx, c->ent_dest,
-                  c->ent_grp, c->layout, c->peers, c->done_ctr, c->seq, c->num_sms,
+                  c->ent_grp, c->layout, c->peers, c->done_ctr, c->seq, c->num_sms, tl_of(c),
                   as_stream(stream));
   // the stage ends when every rank's rows for this rank have landed and sit in
   // their expert-segment rows (one rank: stream order already says so)
   if (c->world > 1) {
     launch_wait_flags(reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->world,
-                      c->world, c->seq, 0u, kErrWaitData, wait_cfg(c), as_stream(stream));
+                      c->world, c->seq, 0u, kErrWaitData, wait_cfg(c), tl_of(c), kTlDataIn,
+                      as_stream(stream));
     launch_fanout(c->dtype, c->H, c->k, c->rank, c->max_tokens, c->layout,
                   reinterpret_cast<const int32_t*>(c->sym + c->off_meta), c->sym + c->off_land,
-                  c->recv_x, c->num_sms, as_stream(stream));
+                  c->recv_x, c->num_sms, tl_of(c), as_stream(stream));
   }
   MEP_CK(c, cudaGetLastError());
   c->stage = 2;
@@ -428,6 +434,7 @@ int mep_expert_ffn(mep_ctx* c, const void* w_in, const void* w_out, int n_local,
   a.tc_single_cta = c->tc_single_cta;
   a.n_local_weights = n_local;
   a.err = c->err_dev;
+  a.tl = tl_of(c);
   // a rank without resident experts still runs the (empty) kernel to signal
   // completion; give the tensor maps a valid base
   if (n_local == 0) {
@@ -453,7 +460,7 @@ int mep_combine(mep_ctx* c, const void* topk_gate, const uint8_t* valid, int64_t
   launch_combine(c->dtype, n, c->k, c->H, c->world, c->sym + c->off_yk, topk_gate, valid, h,
                  residual_multiplier, out, h_out,
                  reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->seq, wait_cfg(c),
-                 c->num_sms, as_stream(stream));
+                 c->num_sms, tl_of(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   c->stage = 0;
   return MEP_OK;
@@ -494,7 +501,7 @@ int mep_rmsnorm(mep_ctx* c, const void* h, const void* w, float eps, int64_t n, 
     return fail(c, MEP_ERR_INVALID, "h, w and x_out must start on 16-byte boundaries");
   if (!(eps >= 0.f)) return fail(c, MEP_ERR_INVALID, "eps must be >= 0");
   if (int rc = use_device(c)) return rc;
-  launch_rmsnorm(c->dtype, n, c->H, h, w, eps, x_out, as_stream(stream));
+  launch_rmsnorm(c->dtype, n, c->H, h, w, eps, x_out, tl_of(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   return MEP_OK;
 }
@@ -574,6 +581,10 @@ int mep_set_option(mep_ctx* c, const char* name, int64_t value) {
     c->tc_single_cta = value != 0;
     return MEP_OK;
   }
+  if (!std::strcmp(name, "timeline")) {
+    c->tl_on = value != 0;
+    return MEP_OK;
+  }
   if (!std::strcmp(name, "timeout_ms")) {
     if (value < 1) return fail(c, MEP_ERR_INVALID, "timeout_ms must be >= 1");
     c->timeout_ns = (unsigned long long)value * 1000000ull;
@@ -588,8 +599,19 @@ int mep_barrier(mep_ctx* c, void* stream) {
   if (int rc = use_device(c)) return rc;
   launch_rank_barrier(c->peers, c->world, c->rank, c->seq + 1,
                       reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), wait_cfg(c),
-                      as_stream(stream));
+                      tl_of(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
+  return MEP_OK;
+}
+
+int mep_read_timeline(mep_ctx* c, uint64_t* out, void* stream) {
+  if (!c || !out) return fail(c, MEP_ERR_INVALID, "NULL argument");
+  if (int rc = use_device(c)) return rc;
+  cudaStream_t st = as_stream(stream);
+  MEP_CK(c, cudaMemcpyAsync(out, c->tl, (size_t)kTlSlots * sizeof(uint64_t),
+                            cudaMemcpyDeviceToHost, st));
+  MEP_CK(c, cudaStreamSynchronize(st));
+  MEP_CK(c, cudaMemsetAsync(c->tl, 0, (size_t)kTlSlots * sizeof(uint64_t), st));
   return MEP_OK;
 }
 
@@ -599,7 +621,7 @@ int mep_debug_wait(mep_ctx* c, uint32_t target, int64_t timeout_ms, void* stream
   if (int rc = use_device(c)) return rc;
   WaitCfg wc{c->err_dev, (unsigned long long)timeout_ms * 1000000ull};
   launch_wait_flags(reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), 0, 1, nullptr,
-                    target, kErrWaitDebug, wc, as_stream(stream));
+                    target, kErrWaitDebug, wc, nullptr, 0, as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   return MEP_OK;
 }

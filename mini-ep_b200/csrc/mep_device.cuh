@@ -43,6 +43,22 @@ __device__ __forceinline__ void set_err(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// Step timeline (profiling, off unless the context's "timeline" option is
+// set): %globaltimer stamps of each stage of a layer step, in nanoseconds.
+// A stage's start is stamped by block 0 when it starts; its end is the
+// latest end over the stage's CTAs (atomicMax, which needs no reset between
+// steps because the timer only grows). Slot numbers are the MEP_TL_* values
+// of include/miniep_b200.h.
+__device__ __forceinline__ void tl_begin(uint64_t* tl, int slot) {
+  if (tl && blockIdx.x == 0 && threadIdx.x == 0) tl[slot] = globaltimer_ns();
+}
+__device__ __forceinline__ void tl_mark(uint64_t* tl, int slot) {
+  if (tl) atomicMax(reinterpret_cast<unsigned long long*>(tl) + slot, globaltimer_ns());
+}
+__device__ __forceinline__ void tl_end(uint64_t* tl, int slot) {
+  if (threadIdx.x == 0) tl_mark(tl, slot);
+}
+
 // Spin until *flag has reached `target` (wrap-safe compare), for at most
 // wc.timeout_ns. Gives up early when another wait already failed, so one
 // missing peer costs one timeout rather than one per kernel. Returns true

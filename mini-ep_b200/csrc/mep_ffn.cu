@@ -91,8 +91,10 @@ __global__ void __launch_bounds__(256) k_ffn_simt(const T* __restrict__ A, int l
                                                   T* __restrict__ act, int act_ld,
                                                   const int32_t* __restrict__ meta, PeerPtrs peers,
                                                   int H, int world, int rank,
-                                                  unsigned int* done_ctr, const uint32_t* seq) {
+                                                  unsigned int* done_ctr, const uint32_t* seq,
+                                                  uint64_t* tl) {
   __shared__ float As[kSimtBK][kSimtBM + 4];
+  tl_begin(tl, MODE == 0 ? kTlGemm1 : kTlGemm2);
   __shared__ float Bs[kSimtBK][kSimtBN + 4];
   __shared__ float Cs[kSimtBM][kSimtBN + 1];
   __shared__ int s_prefix[kMaxExperts + 1], s_base[kMaxExperts], s_rows[kMaxExperts];
@@ -163,6 +165,7 @@ __global__ void __launch_bounds__(256) k_ffn_simt(const T* __restrict__ A, int l
     __syncthreads();
   }
   if (MODE == 1) grid_done_signal_ffn(done_ctr, peers, world, rank, seq);
+  tl_end(tl, (MODE == 0 ? kTlGemm1 : kTlGemm2) + 1);
 }
 
 // =================================================================== tcgen05
@@ -391,6 +394,7 @@ struct TcArgs {
   unsigned int* done_ctr;
   const uint32_t* seq;
   int* err;
+  uint64_t* tl;            // step timeline or null
 };
 
 // MODE 0: GEMM1 + SwiGLU -> act. MODE 1: GEMM2 -> source landing rows.
@@ -407,6 +411,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
   const int wp = warp_id(), lane = lane_id();
   const uint32_t cta = PAIR ? cluster_rank() : 0u;
   const bool leader = cta == 0;
+  tl_begin(args.tl, MODE == 0 ? kTlGemm1 : kTlGemm2);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < G::STAGES; ++s) {
@@ -628,6 +633,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
                    : "memory");
   }
   if (MODE == 1) grid_done_signal_ffn(args.done_ctr, args.peers, args.world, args.rank, args.seq);
+  tl_end(args.tl, (MODE == 0 ? kTlGemm1 : kTlGemm2) + 1);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -694,6 +700,7 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g1.act = static_cast<bf16*>(a.act);
     g1.act_ld = I;
     g1.err = a.err;
+    g1.tl = a.tl;
     const bool pair = !a.tc_single_cta && a.num_sms >= 2;
     // CTA pairs: 2-CTA clusters over an even grid; single CTAs: one per SM
     auto launch = [&](auto kernel, bool as_pair, const CUtensorMap& ta, const CUtensorMap& tb,
@@ -730,6 +737,7 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g2.done_ctr = a.done_ctr;
     g2.seq = a.seq;
     g2.err = a.err;
+    g2.tl = a.tl;
     e = pair ? launch(tc::k_ffn_tc<1, true>, true, tmA2, tmB2, g2)
              : launch(tc::k_ffn_tc<1, false>, false, tmA2, tmB2, g2);
     if (e != cudaSuccess) return (int)e;
@@ -741,20 +749,20 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     k_ffn_simt<bf16, 0><<<grid, 256, 0, st>>>(
         static_cast<const bf16*>(a.recv_x), H, static_cast<const bf16*>(a.w_in), H, 2 * I, I,
         I / 32, a.layout, static_cast<bf16*>(a.act), I, nullptr, a.peers, H, a.world, a.rank,
-        nullptr, a.seq);
+        nullptr, a.seq, a.tl);
     k_ffn_simt<bf16, 1><<<grid, 256, 0, st>>>(
         static_cast<const bf16*>(a.act), I, static_cast<const bf16*>(a.w_out), I, H, 0,
         H / kSimtBN, a.layout, nullptr, 0, a.recv_meta, a.peers, H, a.world, a.rank, a.done_ctr,
-        a.seq);
+        a.seq, a.tl);
   } else {
     k_ffn_simt<float, 0><<<grid, 256, 0, st>>>(
         static_cast<const float*>(a.recv_x), H, static_cast<const float*>(a.w_in), H, 2 * I, I,
         I / 32, a.layout, static_cast<float*>(a.act), I, nullptr, a.peers, H, a.world, a.rank,
-        nullptr, a.seq);
+        nullptr, a.seq, a.tl);
     k_ffn_simt<float, 1><<<grid, 256, 0, st>>>(
         static_cast<const float*>(a.act), I, static_cast<const float*>(a.w_out), I, H, 0,
         H / kSimtBN, a.layout, nullptr, 0, a.recv_meta, a.peers, H, a.world, a.rank,
-        a.done_ctr, a.seq);
+        a.done_ctr, a.seq, a.tl);
   }
   return (int)cudaGetLastError();
 }

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include "miniep_b200.h"
+
 namespace mep {
 
 constexpr int kMaxWorld = 8;      // ranks of one NVLink/NVSwitch box
@@ -15,6 +17,24 @@ constexpr int kRowAlign = 128;    // expert segments in the receive buffer start
 constexpr int kRouteChunkTokens = 256;  // tokens per CTA in the routing scan
 
 enum DType : int { kF32 = 0, kBF16 = 1 };
+
+// Step-timeline slots (the MEP_TL_* values of the public header).
+enum TlSlot : int {
+  kTlBarrierEnd = MEP_TL_BARRIER_END,
+  kTlNorm = MEP_TL_NORM,
+  kTlRouter = MEP_TL_ROUTER,
+  kTlRoute = MEP_TL_ROUTE,
+  kTlCountsSent = MEP_TL_COUNTS_SENT,
+  kTlLayout = MEP_TL_LAYOUT,
+  kTlDispatch = MEP_TL_DISPATCH,
+  kTlDataIn = MEP_TL_DATA_IN,
+  kTlFanout = MEP_TL_FANOUT,
+  kTlGemm1 = MEP_TL_GEMM1,
+  kTlGemm2 = MEP_TL_GEMM2,
+  kTlResultsIn = MEP_TL_RESULTS_IN,
+  kTlCombine = MEP_TL_COMBINE,
+  kTlSlots = MEP_TL_SLOTS,
+};
 
 // Device-side error word values (written to host-mapped memory).
 enum DevErr : int {
@@ -60,13 +80,16 @@ struct WaitCfg {
 };
 
 // ---------------------------------------------------------------- router
+// `tl` (every launcher below that takes it): the step timeline, or null when
+// the context's timeline option is off (mep_device.cuh, tl_begin / tl_end)
 void launch_router(int dtype, const void* x, const void* router_w, const float* bias,
                    int64_t n, int hidden, int experts, int topk, int64_t* idx_out,
-                   void* gate_out, float* logits_out, int num_sms, int* err, cudaStream_t st);
+                   void* gate_out, float* logits_out, int num_sms, int* err, uint64_t* tl,
+                   cudaStream_t st);
 
 // ---------------------------------------------------------------- RMSNorm
 void launch_rmsnorm(int dtype, int64_t n, int hidden, const void* h, const void* w, float eps,
-                    void* x, cudaStream_t st);
+                    void* x, uint64_t* tl, cudaStream_t st);
 
 // ---------------------------------------------------------------- routing
 void launch_route(int64_t n, int topk, int experts, int world, int rank,
@@ -77,7 +100,7 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   uint32_t* seq, unsigned int* sync, int num_sms,
                   const int32_t* cnt_in_local, const uint32_t* flags_local,
                   int64_t* recv_per_layer_l, int64_t cap_rows, Layout* layout, WaitCfg wc,
-                  cudaStream_t st);
+                  uint64_t* tl, cudaStream_t st);
 
 void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids,
                       const int32_t* owners_l, const int32_t* nrep_l, int64_t* rr_l,
@@ -90,27 +113,30 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
                      int64_t max_tokens,
                      const void* x, const int64_t* topk_idx, const int32_t* ent_dest,
                      const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
-                     unsigned int* done_ctr, const uint32_t* seq, int num_sms, cudaStream_t st);
+                     unsigned int* done_ctr, const uint32_t* seq, int num_sms, uint64_t* tl,
+                     cudaStream_t st);
 
 // every rank raises its barrier flag on every peer, then waits (bounded) for all
 void launch_rank_barrier(const PeerPtrs& peers, int world, int rank, uint32_t* bar_seq,
-                         const uint32_t* flags_local, WaitCfg wc, cudaStream_t st);
+                         const uint32_t* flags_local, WaitCfg wc, uint64_t* tl, cudaStream_t st);
 
 // waits for flags [first, first + world) to reach *seq (or `target` when seq is null)
 // Receive rows that came from other ranks: copy each from the landing
 // buffer (row [src][token]) to its expert-segment row.
 void launch_fanout(int dtype, int hidden, int topk, int rank, int64_t max_tokens,
                    const Layout* layout, const int32_t* recv_meta, const void* land,
-                   void* recv_x, int num_sms, cudaStream_t st);
+                   void* recv_x, int num_sms, uint64_t* tl, cudaStream_t st);
 
+// `tl_slot`: timeline slot stamped when the wait ends (ignored when tl is null)
 void launch_wait_flags(const uint32_t* flags_local, int first, int world, const uint32_t* seq,
-                       uint32_t target, int errcode, WaitCfg wc, cudaStream_t st);
+                       uint32_t target, int errcode, WaitCfg wc, uint64_t* tl, int tl_slot,
+                       cudaStream_t st);
 
 void launch_combine(int dtype, int64_t n, int topk, int hidden, int world,
                     const void* yk_local, const void* topk_gate, const uint8_t* valid,
                     const void* h, float residual_multiplier, void* out, void* h_out,
                     const uint32_t* flags_local, const uint32_t* seq, WaitCfg wc, int num_sms,
-                    cudaStream_t st);
+                    uint64_t* tl, cudaStream_t st);
 
 // ---------------------------------------------------------------- expert FFN
 struct FfnArgs {
@@ -131,6 +157,7 @@ struct FfnArgs {
   int tc_single_cta;        // 1: one CTA per 128x256 tile instead of CTA pairs per 256x256
   int n_local_weights;      // leading extent of w_in / w_out
   int* err;                 // host-mapped device error word
+  uint64_t* tl;             // step timeline or null
 };
 // Returns 0 on success, else a cudaError_t value or a negative code.
 int launch_ffn(const FfnArgs& a, cudaStream_t st);

@@ -58,9 +58,11 @@ __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
     int64_t n, int topk, int row_bytes, int world, int rank, int64_t max_tokens,
     const uint8_t* __restrict__ x, const int64_t* __restrict__ topk_idx,
     const int32_t* __restrict__ ent_dest, const int32_t* __restrict__ ent_grp,
-    const Layout* __restrict__ lay, PeerPtrs peers, unsigned int* done_ctr, const uint32_t* seq) {
+    const Layout* __restrict__ lay, PeerPtrs peers, unsigned int* done_ctr, const uint32_t* seq,
+    uint64_t* tl) {
   extern __shared__ __align__(128) uint8_t dsmem[];
   const int lane = lane_id(), wp = warp_id();
+  tl_begin(tl, kTlDispatch);
   uint8_t* bufs = dsmem + (size_t)wp * kDispatchBufs * row_bytes;
   const int64_t stride = (int64_t)gridDim.x * kDispatchWarps;
   const int vec = row_bytes >> 4;
@@ -120,6 +122,7 @@ __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
     asm volatile("fence.proxy.async.global;" ::: "memory");
   }
   grid_done_signal(done_ctr, peers, world, rank, world, seq);
+  tl_end(tl, kTlDispatch + 1);
 }
 
 // Fan-out on the receiver: every receive row whose tag names another rank is
@@ -128,8 +131,9 @@ __global__ void __launch_bounds__(256) k_fanout(int row_bytes, int topk, int ran
                                                 int64_t max_tokens, const Layout* __restrict__ lay,
                                                 const int32_t* __restrict__ meta,
                                                 const uint8_t* __restrict__ land,
-                                                uint8_t* __restrict__ recv_x) {
+                                                uint8_t* __restrict__ recv_x, uint64_t* tl) {
   __shared__ int s_prefix[kMaxExperts + 1], s_base[kMaxExperts], s_rows[kMaxExperts];
+  tl_begin(tl, kTlFanout);
   const int nl = lay->n_local;
   for (int i = threadIdx.x; i <= nl; i += blockDim.x) s_prefix[i] = lay->tile_prefix[i];
   for (int i = threadIdx.x; i < nl; i += blockDim.x) {
@@ -155,23 +159,31 @@ __global__ void __launch_bounds__(256) k_fanout(int row_bytes, int topk, int ran
     uint4* to = reinterpret_cast<uint4*>(recv_x + p * row_bytes);
     for (int c = lane; c < vec; c += 32) to[c] = from[c];
   }
+  tl_end(tl, kTlFanout + 1);
 }
 
 // Rank barrier: raise barrier flag [3W + rank] on every rank to the next
 // barrier number, then wait for all W flags of this rank to reach it.
 __global__ void k_rank_barrier(PeerPtrs peers, int world, int rank, uint32_t* bar_seq,
-                               const uint32_t* flags, WaitCfg wc) {
+                               const uint32_t* flags, WaitCfg wc, uint64_t* tl) {
   const uint32_t s = *bar_seq + 1u;
   if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + 3 * world + rank, s);
   if (threadIdx.x < world) wait_flag(flags + 3 * world + threadIdx.x, s, kErrWaitBarrier, wc);
   __syncthreads();
-  if (threadIdx.x == 0) *bar_seq = s;
+  if (threadIdx.x == 0) {
+    *bar_seq = s;
+    tl_mark(tl, kTlBarrierEnd);
+  }
 }
 
 __global__ void k_wait_flags(const uint32_t* flags, int first, int world, const uint32_t* seq,
-                             uint32_t target, int code, WaitCfg wc) {
+                             uint32_t target, int code, WaitCfg wc, uint64_t* tl, int tl_slot) {
   const uint32_t step = seq ? *seq : target;
   if (threadIdx.x < world) wait_flag(flags + first + threadIdx.x, step, code, wc);
+  if (tl) {
+    __syncthreads();
+    if (threadIdx.x == 0) tl_mark(tl, tl_slot);
+  }
 }
 
 template <typename T>
@@ -248,10 +260,12 @@ __device__ __forceinline__ void combine_body(int64_t n, int topk, int H, int wor
                                              const T* __restrict__ h, float rm,
                                              T* __restrict__ out, T* __restrict__ h_out,
                                              const uint32_t* flags, const uint32_t* seq,
-                                             WaitCfg wc) {
+                                             WaitCfg wc, uint64_t* tl) {
   constexpr int V = Vec16<T>::N;
+  tl_begin(tl, kTlCombine);
   if (threadIdx.x < world) wait_flag(flags + 2 * world + threadIdx.x, *seq, kErrWaitDone, wc);
   __syncthreads();
+  tl_begin(tl, kTlResultsIn);
   const int lane = lane_id();
   const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int nvec = H / V;
@@ -294,6 +308,7 @@ __device__ __forceinline__ void combine_body(int64_t n, int topk, int H, int wor
       }
     }
   }
+  tl_end(tl, kTlCombine + 1);
 }
 
 // top-k <= 8: three CTAs per SM (more slot rows in flight per SM: measured
@@ -307,8 +322,8 @@ __global__ void __launch_bounds__(256, 3) k_combine8(int64_t n, int topk, int H,
                                                      const T* __restrict__ h, float rm,
                                                      T* __restrict__ out, T* __restrict__ h_out,
                                                      const uint32_t* flags, const uint32_t* seq,
-                                                     WaitCfg wc) {
-  combine_body<T, 8>(n, topk, H, world, yk, gate, valid, h, rm, out, h_out, flags, seq, wc);
+                                                     WaitCfg wc, uint64_t* tl) {
+  combine_body<T, 8>(n, topk, H, world, yk, gate, valid, h, rm, out, h_out, flags, seq, wc, tl);
 }
 template <typename T>
 __global__ void __launch_bounds__(256) k_combine16(int64_t n, int topk, int H, int world,
@@ -318,9 +333,9 @@ __global__ void __launch_bounds__(256) k_combine16(int64_t n, int topk, int H, i
                                                    const T* __restrict__ h, float rm,
                                                    T* __restrict__ out, T* __restrict__ h_out,
                                                    const uint32_t* flags, const uint32_t* seq,
-                                                   WaitCfg wc) {
+                                                   WaitCfg wc, uint64_t* tl) {
   combine_body<T, kMaxTopk>(n, topk, H, world, yk, gate, valid, h, rm, out, h_out, flags, seq,
-                            wc);
+                            wc, tl);
 }
 
 }  // namespace
@@ -329,7 +344,7 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
                      int64_t max_tokens, const void* x, const int64_t* topk_idx,
                      const int32_t* ent_dest, const int32_t* ent_grp, const Layout* layout,
                      const PeerPtrs& peers, unsigned int* done_ctr, const uint32_t* seq,
-                     int num_sms, cudaStream_t st) {
+                     int num_sms, uint64_t* tl, cudaStream_t st) {
   const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
   const size_t smem = (size_t)kDispatchWarps * kDispatchBufs * row_bytes;
   static size_t smem_set = 0;
@@ -343,32 +358,33 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
   if (blocks < 1) blocks = 1;
   k_dispatch<<<(unsigned)blocks, 32 * kDispatchWarps, smem, st>>>(
       n, topk, row_bytes, world, rank, max_tokens, static_cast<const uint8_t*>(x), topk_idx,
-      ent_dest, ent_grp, layout, peers, done_ctr, seq);
+      ent_dest, ent_grp, layout, peers, done_ctr, seq, tl);
 }
 
 void launch_fanout(int dtype, int hidden, int topk, int rank, int64_t max_tokens,
                    const Layout* layout, const int32_t* recv_meta, const void* land, void* recv_x,
-                   int num_sms, cudaStream_t st) {
+                   int num_sms, uint64_t* tl, cudaStream_t st) {
   k_fanout<<<(unsigned)num_sms * 8, 256, 0, st>>>(hidden * (dtype == kBF16 ? 2 : 4), topk, rank,
                                                   max_tokens, layout, recv_meta,
                                                   static_cast<const uint8_t*>(land),
-                                                  static_cast<uint8_t*>(recv_x));
+                                                  static_cast<uint8_t*>(recv_x), tl);
 }
 
 void launch_rank_barrier(const PeerPtrs& peers, int world, int rank, uint32_t* bar_seq,
-                         const uint32_t* flags_local, WaitCfg wc, cudaStream_t st) {
-  k_rank_barrier<<<1, 32, 0, st>>>(peers, world, rank, bar_seq, flags_local, wc);
+                         const uint32_t* flags_local, WaitCfg wc, uint64_t* tl, cudaStream_t st) {
+  k_rank_barrier<<<1, 32, 0, st>>>(peers, world, rank, bar_seq, flags_local, wc, tl);
 }
 
 void launch_wait_flags(const uint32_t* flags_local, int first, int world, const uint32_t* seq,
-                       uint32_t target, int errcode, WaitCfg wc, cudaStream_t st) {
-  k_wait_flags<<<1, 32, 0, st>>>(flags_local, first, world, seq, target, errcode, wc);
+                       uint32_t target, int errcode, WaitCfg wc, uint64_t* tl, int tl_slot,
+                       cudaStream_t st) {
+  k_wait_flags<<<1, 32, 0, st>>>(flags_local, first, world, seq, target, errcode, wc, tl, tl_slot);
 }
 
 void launch_combine(int dtype, int64_t n, int topk, int hidden, int world, const void* yk_local,
                     const void* topk_gate, const uint8_t* valid, const void* h,
                     float residual_multiplier, void* out, void* h_out, const uint32_t* flags_local,
-                    const uint32_t* seq, WaitCfg wc, int num_sms, cudaStream_t st) {
+                    const uint32_t* seq, WaitCfg wc, int num_sms, uint64_t* tl, cudaStream_t st) {
   int64_t blocks = (n + 7) / 8;
   if (blocks > (int64_t)num_sms * 8) blocks = (int64_t)num_sms * 8;
   if (blocks < 1) blocks = 1;
@@ -377,7 +393,7 @@ void launch_combine(int dtype, int64_t n, int topk, int hidden, int world, const
   k_combine##KM<T><<<(unsigned)blocks, 256, 0, st>>>(                                       \
       n, topk, hidden, world, static_cast<const T*>(yk_local), static_cast<const T*>(topk_gate), \
       valid, static_cast<const T*>(h), residual_multiplier, static_cast<T*>(out),             \
-      static_cast<T*>(h_out), flags_local, seq, wc)
+      static_cast<T*>(h_out), flags_local, seq, wc, tl)
   static_assert(kMaxTopk == 16, "combine kernels are instantiated for top-8 and top-16");
   if (dtype == kBF16) {
     if (topk <= 8)

@@ -19,8 +19,13 @@
 //     GPU (other streams, other host threads) race and must be serialised
 //     by the caller. Each call writes every scratch word it later reads, so
 //     nothing has to be cleared between calls;
-//   * the first call on each device looks up the array's device address
-//     (cudaGetSymbolAddress); make that first call before any stream capture.
+//   * every call copies the placement from pageable host (stack) memory with
+//     cudaMemcpyAsync, and the first call on each device looks up the
+//     array's device address (cudaGetSymbolAddress): no call may be made
+//     while its stream is being captured;
+//   * an id outside [0, E) gets destination -1 and is left out of the
+//     round-robin advance, as in mep_dest_ranks, but there is no context
+//     error word to report it in: callers validate ids that can be invalid.
 #include <cstdint>
 #include <cstring>
 #include <mutex>

@@ -22,10 +22,11 @@ __device__ __forceinline__ float bf16_bits_hi(uint32_t w) { return __uint_as_flo
 template <typename T, int VPL>
 __global__ void __launch_bounds__(256) k_rmsnorm(int64_t n, int H, const T* __restrict__ h,
                                                  const T* __restrict__ w, float eps,
-                                                 T* __restrict__ x) {
+                                                 T* __restrict__ x, uint64_t* tl) {
   constexpr int V = Pack16<T>::N;
   const int lane = lane_id();
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id();
+  tl_begin(tl, kTlNorm);
   if (row >= n) return;
   const uint4* hr = reinterpret_cast<const uint4*>(h + row * H);
   uint4 v[VPL];
@@ -72,15 +73,17 @@ __global__ void __launch_bounds__(256) k_rmsnorm(int64_t n, int H, const T* __re
     }
     xr[i * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
   }
+  tl_end(tl, kTlNorm + 1);
 }
 
 // any H (multiple of 16 bytes / elements): one warp per row, strided, two passes
 template <typename T>
 __global__ void __launch_bounds__(256) k_rmsnorm_any(int64_t n, int H, const T* __restrict__ h,
                                                      const T* __restrict__ w, float eps,
-                                                     T* __restrict__ x) {
+                                                     T* __restrict__ x, uint64_t* tl) {
   const int lane = lane_id();
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id();
+  tl_begin(tl, kTlNorm);
   if (row >= n) return;
   const T* hr = h + row * H;
   float ss = 0.f;
@@ -94,12 +97,13 @@ __global__ void __launch_bounds__(256) k_rmsnorm_any(int64_t n, int H, const T* 
   const float r = Elt<T>::round(1.0f / sqrtf(Elt<T>::round(mean + eps)));
   for (int c = lane; c < H; c += 32)
     x[row * H + c] = Elt<T>::from_f(Elt<T>::to_f(w[c]) * Elt<T>::round(Elt<T>::to_f(hr[c]) * r));
+  tl_end(tl, kTlNorm + 1);
 }
 
 }  // namespace
 
 void launch_rmsnorm(int dtype, int64_t n, int hidden, const void* h, const void* w, float eps,
-                    void* x, cudaStream_t st) {
+                    void* x, uint64_t* tl, cudaStream_t st) {
   if (n <= 0) return;
   const unsigned grid = (unsigned)((n + 7) / 8);
   if (dtype == kBF16) {
@@ -107,15 +111,15 @@ void launch_rmsnorm(int dtype, int64_t n, int hidden, const void* h, const void*
     auto wb = static_cast<const __nv_bfloat16*>(w);
     auto xb = static_cast<__nv_bfloat16*>(x);
     if (hidden == 1024)
-      k_rmsnorm<__nv_bfloat16, 4><<<grid, 256, 0, st>>>(n, hidden, hb, wb, eps, xb);
+      k_rmsnorm<__nv_bfloat16, 4><<<grid, 256, 0, st>>>(n, hidden, hb, wb, eps, xb, tl);
     else if (hidden == 4096)
-      k_rmsnorm<__nv_bfloat16, 16><<<grid, 256, 0, st>>>(n, hidden, hb, wb, eps, xb);
+      k_rmsnorm<__nv_bfloat16, 16><<<grid, 256, 0, st>>>(n, hidden, hb, wb, eps, xb, tl);
     else
-      k_rmsnorm_any<__nv_bfloat16><<<grid, 256, 0, st>>>(n, hidden, hb, wb, eps, xb);
+      k_rmsnorm_any<__nv_bfloat16><<<grid, 256, 0, st>>>(n, hidden, hb, wb, eps, xb, tl);
   } else {
     k_rmsnorm_any<float><<<grid, 256, 0, st>>>(n, hidden, static_cast<const float*>(h),
                                                 static_cast<const float*>(w), eps,
-                                                static_cast<float*>(x));
+                                                static_cast<float*>(x), tl);
   }
 }
 

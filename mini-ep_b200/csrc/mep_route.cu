@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_rank(
   // chunks (thread i sums chunks i / E, i / E + parts, ...), then add up
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     base[e] = 0;
-    rr_mod[e] = (int)(rr[e] % nrep[e]);
+    rr_mod[e] = (int)(((rr[e] % nrep[e]) + nrep[e]) % nrep[e]);  // >= 0 for any rr
   }
   __syncthreads();
   {
@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     int32_t* __restrict__ chunk_hist, int32_t* __restrict__ ent_dest,
     int32_t* __restrict__ ent_grp, int32_t* __restrict__ my_counts, PeerPtrs peers, uint32_t* seq,
     RouteSync* gs, const int32_t* cnt_in, const uint32_t* flags, int64_t* recv_per_layer,
-    int64_t cap_rows, Layout* lay, WaitCfg wc) {
+    int64_t cap_rows, Layout* lay, WaitCfg wc, uint64_t* tl) {
   __shared__ int hist[kMaxExperts];
   __shared__ int base[kMaxExperts];   // entries of expert e before this CTA's range, then running
   __shared__ int tot[kMaxExperts];
@@ -285,6 +285,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   const int wp = warp_id(), lane = lane_id();
   const int b = blockIdx.x;
   const int64_t t_beg = min((int64_t)b * tpc, n), t_end = min(t_beg + tpc, n);
+  tl_begin(tl, kTlRoute);
 
   // ---- phase 1: round-robin state (read before anyone updates it), local histogram
   if (threadIdx.x == 0) any_rep = 0;
@@ -292,7 +293,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     hist[e] = 0;
     base[e] = 0;
     tot[e] = 0;
-    rr_mod[e] = (int)(rr[e] % nrep[e]);
+    rr_mod[e] = (int)(((rr[e] % nrep[e]) + nrep[e]) % nrep[e]);  // >= 0 for any rr
   }
   __syncthreads();
   for (int64_t f = t_beg * k + threadIdx.x; f < t_end * k; f += blockDim.x) {
@@ -301,7 +302,15 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_hist[(int64_t)b * E + e] = hist[e];
-  grid_barrier(gs, gridDim.x, wc);
+  if (!grid_barrier(gs, gridDim.x, wc)) {
+    // the barrier timed out (error word set): another CTA's histogram may be
+    // missing, so this CTA routes nothing and leaves the round-robin state,
+    // the statistics and the published counts untouched (the peers' bounded
+    // waits then report the step as failed)
+    for (int64_t f = t_beg * k + threadIdx.x; f < t_end * k; f += blockDim.x) ent_dest[f] = -1;
+    tl_end(tl, kTlRoute + 1);
+    return;
+  }
 
   // ---- phase 2: prefix of the earlier CTAs' counts and the totals
   {
@@ -350,11 +359,15 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     __syncthreads();
     if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, step);
     __syncthreads();
-    if (threadIdx.x == 0) *seq = step;
+    if (threadIdx.x == 0) {
+      *seq = step;
+      tl_mark(tl, kTlCountsSent);
+    }
     // the receive layout, once every rank's counts are in (the other CTAs rank meanwhile)
     layout_block(world, rank, E, owners, nrep, cnt_in, flags, recv_per_layer, cap_rows, lay, step,
                  wc);
     __syncthreads();
+    if (threadIdx.x == 0) tl_mark(tl, kTlLayout);
   }
 
   // ---- ranking, 256 tokens per round (8 warps x 32 tokens)
@@ -407,6 +420,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] += hist[e];
     __syncthreads();
   }
+  tl_end(tl, kTlRoute + 1);
 }
 
 __global__ void k_dest_to_i64(int64_t m, const int32_t* __restrict__ d, int64_t* __restrict__ out) {
@@ -423,7 +437,7 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   const PeerPtrs& peers, uint32_t* seq, unsigned int* sync, int num_sms,
                   const int32_t* cnt_in_local, const uint32_t* flags_local,
                   int64_t* recv_per_layer_l, int64_t cap_rows, Layout* layout, WaitCfg wc,
-                  cudaStream_t st) {
+                  uint64_t* tl, cudaStream_t st) {
   // one CTA per 256-token round, at most one per SM (all resident for the grid barrier)
   const int64_t rounds = (n + kRouteChunkTokens - 1) / kRouteChunkTokens;
   int64_t grid = rounds < num_sms ? rounds : num_sms;
@@ -432,7 +446,7 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
   k_route_fused<<<(unsigned)grid, kRouteThreads, 0, st>>>(
       n, topk, experts, tpc, world, rank, topk_idx, valid, owners_l, nrep_l, rr_l, route_counts_l,
       chunk_hist, ent_dest, ent_grp, my_counts, peers, seq, reinterpret_cast<RouteSync*>(sync),
-      cnt_in_local, flags_local, recv_per_layer_l, cap_rows, layout, wc);
+      cnt_in_local, flags_local, recv_per_layer_l, cap_rows, layout, wc, tl);
 }
 
 void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids, const int32_t* owners_l,

@@ -159,9 +159,10 @@ template <int NT>
 __global__ void __launch_bounds__(128) k_router_bf16_mma(
     const bf16* __restrict__ x, const bf16* __restrict__ w, const float* __restrict__ bias,
     int64_t n, int H, int E, int k, int64_t* __restrict__ idx_out, bf16* __restrict__ gate_out,
-    float* __restrict__ logits_out) {
+    float* __restrict__ logits_out, uint64_t* tl) {
   __shared__ float part[4][16][NT * 8 + 1];
   const int wp = warp_id(), lane = lane_id();
+  tl_begin(tl, kTlRouter);
   const int g = lane >> 2, q = lane & 3;
   const int64_t tok0 = (int64_t)blockIdx.x * 16;
   const int ksplit = (H % 256 == 0) ? 4 : 1;
@@ -231,6 +232,7 @@ __global__ void __launch_bounds__(128) k_router_bf16_mma(
     else
       select_topk_warp<bf16>(v[0], v[1], k, tok, idx_out, gate_out);
   }
+  tl_end(tl, kTlRouter + 1);
 }
 
 // CUDA-core router for fp32 (and any shape the tensor-core path does not take):
@@ -239,10 +241,11 @@ template <typename T>
 __global__ void __launch_bounds__(128) k_router_simt(
     const T* __restrict__ x, const T* __restrict__ w, const float* __restrict__ bias, int64_t n,
     int H, int E, int k, int64_t* __restrict__ idx_out, T* __restrict__ gate_out,
-    float* __restrict__ logits_out) {
+    float* __restrict__ logits_out, uint64_t* tl) {
   __shared__ float sl[4][kMaxExperts];
   const int wp = warp_id(), lane = lane_id();
   const int64_t tok = (int64_t)blockIdx.x * 4 + wp;
+  tl_begin(tl, kTlRouter);
   if (tok >= n) return;
   const T* xr = x + tok * H;
   for (int e = lane; e < E; e += 32) {
@@ -258,13 +261,14 @@ __global__ void __launch_bounds__(128) k_router_simt(
       for (int e = 0; e < E; ++e) logits_out[tok * E + e] = v[e];
     select_topk<T>(v, E, k, tok, idx_out, gate_out);
   }
+  tl_end(tl, kTlRouter + 1);
 }
 
 }  // namespace
 
 void launch_router(int dtype, const void* x, const void* router_w, const float* bias, int64_t n,
                    int hidden, int experts, int topk, int64_t* idx_out, void* gate_out,
-                   float* logits_out, int num_sms, int* err, cudaStream_t st) {
+                   float* logits_out, int num_sms, int* err, uint64_t* tl, cudaStream_t st) {
   (void)num_sms;
   (void)err;
   if (n <= 0) return;
@@ -281,7 +285,7 @@ void launch_router(int dtype, const void* x, const void* router_w, const float* 
 #define MEP_ROUTER_CASE(NT)                                                                   \
   case NT:                                                                                   \
     k_router_bf16_mma<NT><<<grid, 128, 0, st>>>(xb, wb, bias, n, hidden, experts, topk, idx_out, \
-                                                gb, logits_out);                             \
+                                                gb, logits_out, tl);                         \
     return;
       MEP_ROUTER_CASE(1)
       MEP_ROUTER_CASE(2)
@@ -299,12 +303,12 @@ void launch_router(int dtype, const void* x, const void* router_w, const float* 
     k_router_simt<bf16><<<grid, 128, 0, st>>>(static_cast<const bf16*>(x),
                                               static_cast<const bf16*>(router_w), bias, n, hidden,
                                               experts, topk, idx_out, static_cast<bf16*>(gate_out),
-                                              logits_out);
+                                              logits_out, tl);
   else
     k_router_simt<float><<<grid, 128, 0, st>>>(static_cast<const float*>(x),
                                                static_cast<const float*>(router_w), bias, n,
                                                hidden, experts, topk, idx_out,
-                                               static_cast<float*>(gate_out), logits_out);
+                                               static_cast<float*>(gate_out), logits_out, tl);
 }
 
 }  // namespace mep

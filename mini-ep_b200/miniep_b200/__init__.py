@@ -8,9 +8,9 @@ include/miniep_b200.h).
 """
 from .ep import (Comm, EPMoEBackend, EPStats, GraphedMoEBlock, LocalMoEBackend,  # noqa: F401
                  Placement, StreamedMoEBlock, router_topk)
-from .balancer import layer_imbalance, plan_balanced, straggler_overhead  # noqa: F401
+from .balancer import layer_imbalance, plan_balanced, plan_lpt, straggler_overhead  # noqa: F401
 from ._lib import MEPError  # noqa: F401
 
 __all__ = ["Comm", "EPMoEBackend", "EPStats", "GraphedMoEBlock", "LocalMoEBackend", "Placement",
            "StreamedMoEBlock", "router_topk",
-           "plan_balanced", "straggler_overhead", "layer_imbalance", "MEPError"]
+           "plan_balanced", "plan_lpt", "straggler_overhead", "layer_imbalance", "MEPError"]

@@ -15,6 +15,12 @@ MEP_OK = 0
 MEP_F32 = 0
 MEP_BF16 = 1
 IPC_HANDLE_BYTES = 64
+# step-timeline slots (MEP_TL_* of include/miniep_b200.h): name -> slot; a
+# stage name has its start at the slot and its end at slot + 1
+TL_SLOTS = 24
+TL_STAGES = {"norm": 1, "router": 3, "route": 5, "dispatch": 9, "fanout": 12, "gemm1": 14,
+             "gemm2": 16, "combine": 19}
+TL_MARKS = {"barrier_end": 0, "counts_sent": 7, "layout": 8, "data_in": 11, "results_in": 18}
 
 _P = C.c_void_p
 _I64 = C.c_int64
@@ -48,6 +54,7 @@ SIGNATURES = {
     "mep_set_option": [_P, C.c_char_p, _I64],
     "mep_debug_wait": [_P, C.c_uint32, _I64, _P],
     "mep_barrier": [_P, _P],
+    "mep_read_timeline": [_P, _P, _P],
     "mep_dest_ranks_noalloc": [_I, _I, _P, _P, _I, _P, _P, _I64, _P, _P],
 }
 _RESTYPES = {"mep_last_error": C.c_char_p}

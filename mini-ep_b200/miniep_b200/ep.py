@@ -186,6 +186,27 @@ class Comm:
         torch.cuda.current_stream(self.device).synchronize()
         check(_lib.lib().mep_check(self._ctx), self._ctx, "device")
 
+    def read_timeline(self) -> dict:
+        """Stamps of the last layer step recorded with the "timeline" option
+        (synchronises, then clears them): {stage: (start_us, end_us)} and
+        {mark: t_us}, in microseconds after this rank's last device barrier
+        (or after the step's first stamp when no barrier ran). Stages that did
+        not run are left out."""
+        buf = (C.c_uint64 * _lib.TL_SLOTS)()
+        check(_lib.lib().mep_read_timeline(self._ctx, buf, _stream()), self._ctx,
+              "mep_read_timeline")
+        raw = list(buf)
+        t0 = raw[_lib.TL_MARKS["barrier_end"]] or min((v for v in raw if v), default=0)
+        us = lambda v: (v - t0) / 1e3  # noqa: E731
+        out = {}
+        for name, s in _lib.TL_STAGES.items():
+            if raw[s] and raw[s + 1]:
+                out[name] = (us(raw[s]), us(raw[s + 1]))
+        for name, s in _lib.TL_MARKS.items():
+            if raw[s] and name != "barrier_end":
+                out[name] = us(raw[s])
+        return out
+
     def last_recv_rows(self) -> int:
         v = C.c_int64()
         check(_lib.lib().mep_last_recv_rows(self._ctx, C.byref(v), _stream()), self._ctx)
@@ -398,6 +419,24 @@ class EPMoEBackend:
         return h_out.view_as(h), idx, gate, x
 
 
+def _captured_state(backend: "EPMoEBackend") -> tuple:
+    """What a captured layer step bakes into its CUDA graph from the backend:
+    the expert weight addresses, the resident-expert list and the placement
+    object (the tables the graph's kernels read are uploaded per placement)."""
+    return (backend.w_in.data_ptr(), backend.w_out.data_ptr(), tuple(backend.local_experts),
+            id(backend.placement))
+
+
+def _check_replay(backend: "EPMoEBackend", captured: tuple):
+    """Refuse to replay a graph whose backend changed since capture (a
+    re-placement swaps the weight tensors, the expert list and the tables;
+    the graph would read freed weights with a stale expert count)."""
+    if _captured_state(backend) != captured:
+        raise MEPError(f"layer {backend.layer}: the backend's placement or expert weights "
+                       "changed since this graphed block was captured (a re-placement); "
+                       "build a new GraphedMoEBlock / StreamedMoEBlock")
+
+
 class GraphedMoEBlock:
     """The MoE half of ``Block.forward`` (router + expert-parallel layer +
     residual, miniep/modeling.py:192-197) for a fixed token count, captured once
@@ -436,6 +475,7 @@ class GraphedMoEBlock:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._step()
+        self.captured = _captured_state(backend)
 
     def _step(self):
         be, comm = self.backend, self.backend.comm
@@ -462,6 +502,7 @@ class GraphedMoEBlock:
             self.x.copy_(x, non_blocking=True)
         if h is not None:
             self.h.copy_(h, non_blocking=True)
+        _check_replay(self.backend, self.captured)
         self.graph.replay()
         return self.h_out
 
@@ -563,6 +604,8 @@ class StreamedMoEBlock:
         stream. The host tensors must be pinned for the copies to overlap;
         ``out_host`` is complete once the current stream reaches this point."""
         self._check(x_host, h_host, out_host)
+        for blk in self.blocks:
+            _check_replay(blk.backend, blk.captured)
         if getattr(self, "graph", None) is not None and self.bound == (
                 None if x_host is None else x_host.data_ptr(), h_host.data_ptr(),
                 out_host.data_ptr()):

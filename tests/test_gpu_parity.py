@@ -20,6 +20,10 @@ pytestmark = pytest.mark.gpu
 
 FP32_RTOL = 1e-5       # fp32 outputs: max|gpu - ref| <= 1e-5 * max|ref|
 BF16_ATOL = 2e-2       # bf16 outputs vs an fp32 reference, max-abs, for outputs of unit scale
+# Tie-free rows whose top-k may differ from the reference's because one bf16
+# logit rounded a step the other way (fp32 sums of the router GEMM in another
+# order than torch's CPU kernel): at most this fraction of the rows.
+ROUTER_ROUNDING_ROWS = 0.02
 
 
 def bf16_tol(ref32):
@@ -80,8 +84,17 @@ def test_router_bf16_skewed(shape, n):
         assert same_row.float().mean() > 0.9
     # selection rule is exact on the kernel's own logits (lower index first on ties)
     assert torch.equal(idx, O.topk_lowest_index(logits, sh["topk"]))
-    # against the reference: bit-exact wherever the logits agree and hold no tie
-    ok = same_row & ~O.boundary_ties(ref_logits, sh["topk"])
+    # against the reference, every row without an exact tie in its top-(k+1)
+    # logits (where torch's CPU topk has no fixed order) is compared
+    ties = O.boundary_ties(ref_logits, sh["topk"])
+    off = ~(idx == ref_idx).all(dim=1) & ~ties
+    # a row whose logits equal the reference's bit for bit selects the same experts
+    assert not (off & same_row).any()
+    # the rest: a logit one rounding step from the reference's moved the choice
+    # (reported apart; bounded by ROUTER_ROUNDING_ROWS of the tie-free rows)
+    assert int(off.sum()) <= ROUTER_ROUNDING_ROWS * int((~ties).sum()), \
+        (int(off.sum()), int((~ties).sum()))
+    ok = ~ties & ~off
     assert torch.equal(idx[ok], ref_idx[ok])
     assert torch.equal(logits.gather(1, idx)[same_row],
                        ref_logits.float().gather(1, ref_idx)[same_row])
@@ -89,6 +102,8 @@ def test_router_bf16_skewed(shape, n):
     # per-expert histogram of the kernel's routing == the reference's on tie-free rows
     assert torch.equal(torch.bincount(idx[ok].reshape(-1), minlength=sh["experts"]),
                        torch.bincount(ref_idx[ok].reshape(-1), minlength=sh["experts"]))
+    print(f"router {shape} n={n}: exact-tie rows {int(ties.sum())}, "
+          f"rounding-moved rows {int(off.sum())} of {int((~ties).sum())} tie-free")
 
 
 def test_dispatch_rejects_rows_not_16_byte_aligned():
@@ -249,8 +264,15 @@ def test_moe_block_matches_reference_block(golden):
     h_out, idx, gate = be.moe_block(h.cuda(), lb.x.cuda(), lb.router.cuda(),
                                     synth.GRANITE_RESIDUAL_MULTIPLIER, bias=bias.cuda())
     ref_idx = torch.from_numpy(g["topk_idx"]).long()
-    same = (idx.cpu().sort(1).values == ref_idx.sort(1).values).all(dim=1)
-    assert same.float().mean() > 0.5  # the rest differ only by the order of exact ties
+    # rows without an exact tie in the reference's top-(k+1) logits select the
+    # reference's experts in the reference's order; a row with such a tie may
+    # order the tied experts differently (torch's CPU topk has no tie rule)
+    ties = O.boundary_ties(_bf16(g["logits"]).float(), sh["topk"])
+    same = (idx.cpu() == ref_idx).all(dim=1)
+    off = ~same & ~ties
+    assert int(off.sum()) <= ROUTER_ROUNDING_ROWS * int((~ties).sum()), int(off.sum())
+    same = same & ~ties
+    assert int(same.sum()) >= 0.75 * 128
     d = (h_out.cpu().float() - _bf16(g["block_out"]).float()).abs()
     assert d[same].max() <= BF16_ATOL
     # rows with a different tie pick still equal h + rm * moe(x) of their own routing

@@ -80,7 +80,16 @@ def _worker(rank, world, port, out_dir):
         mine = old.experts_of_rank(rank)[l]
         backends.append(EPMoEBackend(l, comm, old, mine, w_in_all[l][mine].clone(),
                                      w_out_all[l][mine].clone(), stats))
+    caps = [ep._captured_state(be) for be in backends]  # what graphed blocks would hold
     res = rebalance(backends, stats, slots_per_rank=2)
+    stale = []
+    for be, cap in zip(backends, caps):
+        try:
+            ep._check_replay(be, cap)
+            stale.append(False)
+        except _lib.MEPError:
+            stale.append(True)
+    ep._check_replay(backends[0], ep._captured_state(backends[0]))  # a fresh capture replays
     new = backends[0].placement
     ok = []
     for l, be in enumerate(backends):
@@ -89,7 +98,7 @@ def _worker(rank, world, port, out_dir):
                   and torch.equal(be.w_out, w_out_all[l][mine]))
     out = dict(plan=res["plan"], ok=ok, moved=res["moved_experts"], tables=fake.tables,
                resets=fake.resets, installed=comm.placement is new,
-               replicas=res["replicas_added"])
+               replicas=res["replicas_added"], stale=stale)
     Path(out_dir, f"r{rank}.json").write_text(json.dumps(out))
     dist.destroy_process_group()
 
@@ -110,3 +119,5 @@ def test_rebalance_moves_weights_between_gloo_ranks(tmp_path):
         assert all(r["ok"])
         assert r["installed"] and r["resets"] == 1
         assert r["tables"][-2:] == [0, 1]
+        # graphs captured before the re-placement refuse to replay after it
+        assert r["stale"] == [True, True]
