@@ -266,6 +266,15 @@ def run_reference(a):
 
 
 # --------------------------------------------------------------- GPU leg
+_T0 = time.perf_counter()
+
+
+def progress(rank: int, what: str):
+    """One stderr line per phase (rank, seconds since start): where a run
+    that stalls stopped."""
+    print(f"[bench r{rank} {time.perf_counter() - _T0:7.1f}s] {what}", file=sys.stderr, flush=True)
+
+
 def make_plan(kind, counts, world, slots):
     from miniep_b200 import Placement, plan_balanced, plan_lpt
     E = counts.numel()
@@ -315,6 +324,7 @@ def main_b200(a):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    progress(rank, "process group up")
     clocks = ClockSampler(local)
     clocks.start()
     sh = synth.SHAPES[a.shape]
@@ -342,6 +352,7 @@ def main_b200(a):
     if world > 1:
         dist.all_reduce(counts)
     placement, plan_report = make_plan(a.plan, counts, world, a.slots)
+    progress(rank, f"plan {a.plan}: experts {placement.experts_of_rank(rank)[0]}")
     comm.install(placement)
     mine = placement.experts_of_rank(rank)[0]
     w_in, w_out = lt.w_in[mine].contiguous(), lt.w_out[mine].contiguous()
@@ -411,6 +422,7 @@ def main_b200(a):
     torch.cuda.synchronize()
     comm.check()
 
+    progress(rank, "warm-up done")
     # 1) eager stages: FFN-stage time for the roofline, and the eager step time
     n_eager = max(10, min(a.steps // 4, 50))
     ffn = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -420,6 +432,7 @@ def main_b200(a):
     recv_rows = comm.last_recv_rows()
     comm.check()
 
+    progress(rank, "eager stages timed")
     # 2) the step as one CUDA graph (GraphedMoEBlock): the reported value
     blk = GraphedMoEBlock(be, n, router_w, rm, bias=bias, norm_w=nw, eps=NORM_EPS)
     blk.h.copy_(h)
@@ -439,6 +452,7 @@ def main_b200(a):
     snap = stats.snapshot()  # route counts and received entries of the timed steps
     timed_recv = snap["recv_tokens"] / a.steps
 
+    progress(rank, f"graphed steps timed: {ms_step:.3f} ms")
     # 3) timeline: per-stage device stamps of the graphed step on every rank
     stages = None
     if a.timeline_steps > 0:
@@ -467,6 +481,7 @@ def main_b200(a):
             else:
                 stages[key] = round(statistics.median(vals), 1)
 
+    progress(rank, "timeline done")
     # 4) e2e: the public graphed API with host buffers, copies inside the timed region
     e2e = None
     if not a.no_e2e:
@@ -508,6 +523,7 @@ def main_b200(a):
         del sblk
     clk = clocks.stop()
 
+    progress(rank, "e2e done")
     # 5) one checked step: round-robin state reset, so the checker can follow it
     parity_in = None
     if not a.no_parity:
@@ -524,6 +540,7 @@ def main_b200(a):
                      "gate": p_gate[rows.to(dev)].cpu(), "out": p_out[rows.to(dev)].cpu()}
         del p_out, p_idx, p_gate, p_x
 
+    progress(rank, "checked step done")
     # gather the per-rank figures on rank 0
     per_rank = {"rank": rank, "recv_rows": recv_rows, "timed_recv_per_step": timed_recv,
                 "ffn_ms": sum(ffn_ms) / n_eager, "step_ms": sum(step_ms) / a.steps,
@@ -534,6 +551,7 @@ def main_b200(a):
     else:
         got = [per_rank]
 
+    progress(rank, "gathered")
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline(sh, a.tokens, a.cpu_seconds)
