@@ -80,6 +80,8 @@ def parse():
     ap.add_argument("--e2e-chunks", type=int, default=0,
                     help="pieces per host batch in the e2e leg (0: 4 from 4096 tokens per rank, else 2)")
     ap.add_argument("--force-simt", action="store_true")
+    ap.add_argument("--dispatch-per-warp", action="store_true",
+                    help="dispatch with one warp per token instead of the streaming engine")
     ap.add_argument("--e2e-graph", choices=["on", "off"], default="off",
                     help="capture the e2e host pipeline as one CUDA graph per step "
                          "(measured slower at N=1 and 2: consecutive steps stop overlapping)")
@@ -344,6 +346,8 @@ def main_b200(a):
                 dtype=torch.bfloat16, device=local, timeout_ms=20000)
     if a.force_simt:
         comm.set_option("force_simt", 1)
+    if a.dispatch_per_warp:
+        comm.set_option("dispatch_per_warp", 1)
     from miniep_b200 import Placement
     comm.install(Placement.naive(1, E, world))
     # profiling pass: the global per-expert load of these tokens

@@ -15,9 +15,9 @@ struct mep_ctx {
   int64_t max_tokens = 0, cap_rows = 0;
   int num_sms = 0;
   size_t elt = 4;
-  // symmetric region (exported over CUDA IPC): flags | counts | meta | land | yk
+  // symmetric region (exported over CUDA IPC): flags | counts | meta | land | ret
   uint8_t* sym = nullptr;
-  size_t sym_bytes = 0, off_flags = 0, off_cnt = 0, off_meta = 0, off_land = 0, off_yk = 0;
+  size_t sym_bytes = 0, off_flags = 0, off_cnt = 0, off_meta = 0, off_land = 0, off_ret = 0;
   void* recv_x = nullptr;  // expert-grouped receive rows (local only)
   uint8_t* peer_base[kMaxWorld] = {};
   bool peer_open[kMaxWorld] = {};
@@ -43,6 +43,7 @@ struct mep_ctx {
   unsigned long long timeout_ns = 10ull * 1000 * 1000 * 1000;
   int force_simt = 0;
   int tc_single_cta = 0;
+  int dispatch_per_warp = 0;  // 1: one warp per token (k_dispatch) instead of the streaming engine
   std::vector<int> placed, n_local_l;
   int cur_layer = -1, stage = 0;
   int64_t cur_n = 0;
@@ -79,7 +80,7 @@ void build_peers(mep_ctx* c) {
     c->peers.land[r] = b ? b + c->off_land : nullptr;
     c->peers.recv_x[r] = r == c->rank ? c->recv_x : nullptr;  // only this rank's rows are stored here
     c->peers.recv_meta[r] = b ? reinterpret_cast<int32_t*>(b + c->off_meta) : nullptr;
-    c->peers.yk[r] = b ? b + c->off_yk : nullptr;
+    c->peers.ret[r] = b ? b + c->off_ret : nullptr;
     c->peers.cnt_in[r] = b ? reinterpret_cast<int32_t*>(b + c->off_cnt) : nullptr;
     c->peers.flags[r] = b ? reinterpret_cast<uint32_t*>(b + c->off_flags) : nullptr;
   }
@@ -191,7 +192,7 @@ int mep_ctx_create(int rank, int world, int device, int num_layers, int num_expe
   off = align_up(off + (size_t)c->cap_rows * sizeof(int32_t), 1024);
   c->off_land = off;  // [src rank][max_tokens][H]: each token row once per destination rank
   off = align_up(off + (size_t)(world > 1 ? world : 0) * max_tokens * hidden * elt, 1024);
-  c->off_yk = off;
+  c->off_ret = off;  // return rows: one per entry of this rank's tokens
   off = align_up(off + (size_t)max_tokens * topk * hidden * elt, 1024);
   c->sym_bytes = off;
 
@@ -389,8 +390,8 @@ int mep_dispatch(mep_ctx* c, const void* x, const int64_t* topk_idx, int64_t n, 
   // the receive layout was computed by mep_route's kernel
   launch_dispatch(c->dtype, n, c->k, c->H, c->world, c->rank, c->max_tokens,
                   x, topk_idx, c->ent_dest,
-                  c->ent_grp, c->layout, c->peers, c->done_ctr, c->seq, c->num_sms, tl_of(c),
-                  as_stream(stream));
+                  c->ent_grp, c->layout, c->peers, c->done_ctr, c->seq, c->num_sms,
+                  c->dispatch_per_warp, c->err_dev, tl_of(c), as_stream(stream));
   // the stage ends when every rank's rows for this rank have landed and sit in
   // their expert-segment rows (one rank: stream order already says so)
   if (c->world > 1) {
@@ -421,7 +422,7 @@ int mep_expert_ffn(mep_ctx* c, const void* w_in, const void* w_out, int n_local,
   a.rank = c->rank;
   a.cap_rows = c->cap_rows;
   a.recv_x = c->recv_x;
-  a.recv_meta = reinterpret_cast<const int32_t*>(c->sym + c->off_meta);
+  a.ret_rows = c->max_tokens * c->k;
   a.act = c->act;
   a.w_in = w_in;
   a.w_out = w_out;
@@ -457,7 +458,9 @@ int mep_combine(mep_ctx* c, const void* topk_gate, const uint8_t* valid, int64_t
   if (n > 0 && !out && !h_out) return fail(c, MEP_ERR_INVALID, "no output given");
   if (h_out && !h) return fail(c, MEP_ERR_INVALID, "h_out needs h");
   if (int rc = use_device(c)) return rc;
-  launch_combine(c->dtype, n, c->k, c->H, c->world, c->sym + c->off_yk, topk_gate, valid, h,
+  // ent_grp holds each entry's return row since the dispatch
+  launch_combine(c->dtype, n, c->k, c->H, c->world, c->sym + c->off_ret, c->ent_grp, topk_gate,
+                 valid, h,
                  residual_multiplier, out, h_out,
                  reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->seq, wait_cfg(c),
                  c->num_sms, tl_of(c), as_stream(stream));
@@ -579,6 +582,10 @@ int mep_set_option(mep_ctx* c, const char* name, int64_t value) {
   }
   if (!std::strcmp(name, "tc_single_cta")) {
     c->tc_single_cta = value != 0;
+    return MEP_OK;
+  }
+  if (!std::strcmp(name, "dispatch_per_warp")) {
+    c->dispatch_per_warp = value != 0;
     return MEP_OK;
   }
   if (!std::strcmp(name, "timeline")) {

@@ -104,6 +104,44 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+// Bounded parity wait on a CTA-local mbarrier: false after timeout_ns (or
+// once *abort is set by another warp of the CTA that gave up).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* b, uint32_t parity,
+                                              unsigned long long timeout_ns,
+                                              volatile int* abort) {
+  if (mbar_try(b, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try(b, parity)) return true;
+    if ((it & 63u) == 63u) {
+      if (abort && *abort) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        if (abort) *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+// Bulk copy of `bytes` from global memory into this CTA's shared memory,
+// completing (complete_tx) on mbarrier `bar`.
+__device__ __forceinline__ void bulk_load_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Bulk copy of `bytes` from shared memory to global memory (local or a
+// peer's), in the issuing thread's current bulk group.
+__device__ __forceinline__ void bulk_store_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 

@@ -20,6 +20,7 @@
 //     halves of the SwiGLU for the same rows.
 //   * CUDA cores (fp32, and bf16 when asked): 64x64 register-tiled FMA kernel.
 #include <cstdint>
+#include <cstring>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include "mep_device.cuh"
@@ -89,7 +90,7 @@ __global__ void __launch_bounds__(256) k_ffn_simt(const T* __restrict__ A, int l
                                                   int b_rows_per_expert, int b_up_off,
                                                   int ntiles_n, const Layout* __restrict__ lay,
                                                   T* __restrict__ act, int act_ld,
-                                                  const int32_t* __restrict__ meta, PeerPtrs peers,
+                                                  PeerPtrs peers,
                                                   int H, int world, int rank,
                                                   unsigned int* done_ctr, const uint32_t* seq,
                                                   uint64_t* tl) {
@@ -153,11 +154,16 @@ __global__ void __launch_bounds__(256) k_ffn_simt(const T* __restrict__ A, int l
         }
       }
     } else {
+      // row -> (source rank, row of its return buffer)
+      const int* sb = lay->src_begin + c.j * (kMaxWorld + 1);
+      const int* rr = lay->ret_row + c.j * kMaxWorld;
       for (int i = tid; i < kSimtBM * kSimtBN; i += 256) {
         const int r = i / kSimtBN, cc = i % kSimtBN;
         if (r < c.rows) {
-          const int32_t mt = meta[c.row0 + r];
-          T* dst = static_cast<T*>(peers.yk[mt >> 24]) + (int64_t)(mt & 0xffffff) * H;
+          const int lr = c.row0 - s_base[c.j] + r;
+          int src = 0;
+          while (src + 1 < world && sb[src + 1] <= lr) ++src;
+          T* dst = static_cast<T*>(peers.ret[src]) + (int64_t)(rr[src] + lr - sb[src]) * H;
           dst[c.nb * kSimtBN + cc] = Elt<T>::from_f(Cs[r][cc]);
         }
       }
@@ -205,8 +211,8 @@ struct Smem {
 // epilogue staging: 32 rows x 128 B per warp, 16-byte chunks XOR-swizzled by row
 constexpr int STAGE_WARP_BYTES = 32 * 128;
 template <bool PAIR>
-__host__ __device__ constexpr int off_stage() {
-  return Geo<PAIR>::DATA + (((int)sizeof(Smem<PAIR>) + 127) / 128) * 128;
+__host__ __device__ constexpr int off_stage() {  // 1024-aligned: TMA 128B-swizzle tile source
+  return Geo<PAIR>::DATA + (((int)sizeof(Smem<PAIR>) + 1023) / 1024) * 1024;
 }
 template <bool PAIR>
 __host__ __device__ constexpr int smem_bytes() {
@@ -266,6 +272,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
         " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
         : "memory");
+}
+// 2D TMA tile store from this CTA's shared memory (128B-swizzled rows), in
+// the issuing thread's bulk group
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::
+                   "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
 }
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
@@ -379,6 +392,12 @@ __device__ __forceinline__ void warp_store_rows(uint8_t* stage, const uint32_t (
   __syncwarp();
 }
 
+// Tensor maps of every rank's return buffer (rows of H bf16, boxes of 32
+// rows x 64 columns, 128B swizzle): GEMM2's tile stores
+struct RetMaps {
+  CUtensorMap m[kMaxWorld];
+};
+
 struct TcArgs {
   const Layout* lay;
   int K;                   // reduction length
@@ -388,7 +407,6 @@ struct TcArgs {
   int b_second;            // offset of the second 128-row half of the B tile
   bf16* act;               // MODE 0 output
   int act_ld;
-  const int32_t* meta;     // MODE 1: (src << 24) | entry per receive row
   PeerPtrs peers;
   int H, world, rank;
   unsigned int* done_ctr;
@@ -402,6 +420,7 @@ struct TcArgs {
 template <int MODE, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ CUtensorMap tmA,
                                                        const __grid_constant__ CUtensorMap tmB,
+                                                       const __grid_constant__ RetMaps rmaps,
                                                        const TcArgs args) {
   using G = Geo<PAIR>;
   extern __shared__ uint8_t smem_raw[];
@@ -556,8 +575,20 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
       const int r = (int)cta * 128 + m;  // row inside the tile
       const bool valid = r < c.rows;
       const int64_t grow = c.row0 + r;
-      int32_t mt = 0;
-      if (MODE == 1 && valid) mt = args.meta[grow];  // in flight while the accumulator fills
+      // MODE 1: this warp's 32 rows [lr0, lr0 + 32) of the segment; the source
+      // of the first and whether all 32 are that source's (looked up while the
+      // accumulator fills)
+      int src = 0, src_end = 0, drow = 0, lr0 = 0;
+      const int* sb = nullptr;
+      const int* rr = nullptr;
+      if (MODE == 1) {
+        sb = args.lay->src_begin + c.j * (kMaxWorld + 1);
+        rr = args.lay->ret_row + c.j * kMaxWorld;
+        lr0 = c.row0 - S->base[c.j] + (int)cta * 128 + q * 32;
+        while (src + 1 < args.world && __ldg(sb + src + 1) <= lr0) ++src;
+        src_end = __ldg(sb + src + 1);
+        drow = __ldg(rr + src) + (lr0 - __ldg(sb + src));
+      }
       // one lane waits, the warp follows its verdict: the TMEM loads below are
       // warp-collective, so the warp must never split on a timeout
       int ok = 1;
@@ -609,12 +640,51 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
         bf16* row = valid ? args.act + grow * args.act_ld + c.nb * 128 + h * 64 : nullptr;
         warp_store_rows(stage, packed[0], row, lane);
       } else {
-        bf16* row = valid ? static_cast<bf16*>(args.peers.yk[mt >> 24]) +
-                                (int64_t)(mt & 0xffffff) * args.H + c.nb * BN + h * 128
-                          : nullptr;
-        warp_store_rows(stage, packed[0], row, lane);
-        warp_store_rows(stage, packed[1], row ? row + 64 : nullptr, lane);
+        const int col0 = c.nb * BN + h * 128;
+        if (lane == 0)  // the staging area's previous tile stores have read it
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncwarp();
+        if (lr0 + 32 <= src_end) {
+          // one source's contiguous rows: two 32 x 64 tile stores into its
+          // return buffer (a peer's over NVLink), issued by one lane
+#pragma unroll
+          for (int c64 = 0; c64 < 2; ++c64) {
+            if (c64) {
+              if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+              __syncwarp();
+            }
+            uint8_t* srow = stage + lane * 128;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              *reinterpret_cast<uint4*>(srow + ((i ^ (lane & 7)) << 4)) =
+                  make_uint4(packed[c64][4 * i], packed[c64][4 * i + 1], packed[c64][4 * i + 2],
+                             packed[c64][4 * i + 3]);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&rmaps.m[src], stage, col0 + c64 * 64, drow);
+              asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
+          }
+        } else {
+          // the chunk crosses a source boundary or the segment's end: row by row
+          const int lr = lr0 + lane;
+          bf16* row = nullptr;
+          if (lr < S->rows[c.j]) {
+            int s2 = src;
+            while (s2 + 1 < args.world && __ldg(sb + s2 + 1) <= lr) ++s2;
+            row = static_cast<bf16*>(args.peers.ret[s2]) +
+                  (int64_t)(__ldg(rr + s2) + lr - __ldg(sb + s2)) * args.H + col0;
+          }
+          warp_store_rows(stage, packed[0], row, lane);
+          warp_store_rows(stage, packed[1], row ? row + 64 : nullptr, lane);
+        }
       }
+    }
+    if (MODE == 1 && lane == 0) {
+      // every tile store has written its rows before the completion signal
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      asm volatile("fence.proxy.async.global;" ::: "memory");
     }
   }
 
@@ -703,6 +773,12 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g1.tl = a.tl;
     const bool pair = !a.tc_single_cta && a.num_sms >= 2;
     // CTA pairs: 2-CTA clusters over an even grid; single CTAs: one per SM
+    // GEMM2's tile stores: every rank's return buffer (ranks past world: unused)
+    tc::RetMaps rmaps;
+    std::memset(&rmaps, 0, sizeof(rmaps));
+    for (int r = 0; r < a.world; ++r)
+      if ((rc = tc::make_tmap(&rmaps.m[r], a.peers.ret[r], H, (uint64_t)a.ret_rows, 32)))
+        return rc;
     auto launch = [&](auto kernel, bool as_pair, const CUtensorMap& ta, const CUtensorMap& tb,
                       const tc::TcArgs& g) -> cudaError_t {
       cudaLaunchConfig_t cfg{};
@@ -717,7 +793,7 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
       attr[0].val.clusterDim.z = 1;
       cfg.attrs = attr;
       cfg.numAttrs = as_pair ? 1 : 0;
-      return cudaLaunchKernelEx(&cfg, kernel, ta, tb, g);
+      return cudaLaunchKernelEx(&cfg, kernel, ta, tb, rmaps, g);
     };
     cudaError_t e = pair ? launch(tc::k_ffn_tc<0, true>, true, tmA1, tmB1, g1)
                          : launch(tc::k_ffn_tc<0, false>, false, tmA1, tmB1, g1);
@@ -729,7 +805,6 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g2.b_rows_per_expert = H;
     g2.b_step = tc::BN;
     g2.b_second = 128;
-    g2.meta = a.recv_meta;
     g2.peers = a.peers;
     g2.H = H;
     g2.world = a.world;
@@ -748,20 +823,20 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
   if (a.dtype == kBF16) {
     k_ffn_simt<bf16, 0><<<grid, 256, 0, st>>>(
         static_cast<const bf16*>(a.recv_x), H, static_cast<const bf16*>(a.w_in), H, 2 * I, I,
-        I / 32, a.layout, static_cast<bf16*>(a.act), I, nullptr, a.peers, H, a.world, a.rank,
+        I / 32, a.layout, static_cast<bf16*>(a.act), I, a.peers, H, a.world, a.rank,
         nullptr, a.seq, a.tl);
     k_ffn_simt<bf16, 1><<<grid, 256, 0, st>>>(
         static_cast<const bf16*>(a.act), I, static_cast<const bf16*>(a.w_out), I, H, 0,
-        H / kSimtBN, a.layout, nullptr, 0, a.recv_meta, a.peers, H, a.world, a.rank, a.done_ctr,
+        H / kSimtBN, a.layout, nullptr, 0, a.peers, H, a.world, a.rank, a.done_ctr,
         a.seq, a.tl);
   } else {
     k_ffn_simt<float, 0><<<grid, 256, 0, st>>>(
         static_cast<const float*>(a.recv_x), H, static_cast<const float*>(a.w_in), H, 2 * I, I,
-        I / 32, a.layout, static_cast<float*>(a.act), I, nullptr, a.peers, H, a.world, a.rank,
+        I / 32, a.layout, static_cast<float*>(a.act), I, a.peers, H, a.world, a.rank,
         nullptr, a.seq, a.tl);
     k_ffn_simt<float, 1><<<grid, 256, 0, st>>>(
         static_cast<const float*>(a.act), I, static_cast<const float*>(a.w_out), I, H, 0,
-        H / kSimtBN, a.layout, nullptr, 0, a.recv_meta, a.peers, H, a.world, a.rank,
+        H / kSimtBN, a.layout, nullptr, 0, a.peers, H, a.world, a.rank,
         a.done_ctr, a.seq, a.tl);
   }
   return (int)cudaGetLastError();

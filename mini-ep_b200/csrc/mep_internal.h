@@ -62,6 +62,14 @@ struct Layout {
   int tile_prefix[kMaxExperts + 1];  // first 128-row tile of local expert j
   int local_expert[kMaxExperts];     // global id of local expert j
   int dst_off[kMaxWorld * kMaxExperts];  // [d][e]: first row this rank writes at rank d for expert e
+  // Return buffer. Every rank receives its entries' expert outputs in (owner
+  // rank d, expert e, index within the (d, e) group) order:
+  int ret_off[kMaxWorld * kMaxExperts];  // [d][e]: first return row of the (d, e) group here
+  // owner side, per local segment j: rows from source s start at row
+  // src_begin[j][s] of the segment (src_begin[j][world] = the segment's
+  // rows) and go to row ret_row[j][s] of source s's return buffer
+  int src_begin[kMaxExperts * (kMaxWorld + 1)];
+  int ret_row[kMaxExperts * kMaxWorld];
 };
 
 // Pointers every rank can reach (own and peers' symmetric buffers).
@@ -69,7 +77,7 @@ struct PeerPtrs {
   void* recv_x[kMaxWorld];     // expert-grouped receive rows
   void* land[kMaxWorld];       // token landing buffers: [src rank][max_tokens][H]
   int32_t* recv_meta[kMaxWorld];
-  void* yk[kMaxWorld];
+  void* ret[kMaxWorld];        // return buffers: expert outputs in (owner, expert, group) order
   int32_t* cnt_in[kMaxWorld];
   uint32_t* flags[kMaxWorld];  // [0,W) counts, [W,2W) data, [2W,3W) done, [3W,4W) barrier
 };
@@ -112,9 +120,9 @@ void launch_dest_only(int64_t m, int experts, const int64_t* expert_ids,
 void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int rank,
                      int64_t max_tokens,
                      const void* x, const int64_t* topk_idx, const int32_t* ent_dest,
-                     const int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
-                     unsigned int* done_ctr, const uint32_t* seq, int num_sms, uint64_t* tl,
-                     cudaStream_t st);
+                     int32_t* ent_grp, const Layout* layout, const PeerPtrs& peers,
+                     unsigned int* done_ctr, const uint32_t* seq, int num_sms, int per_warp,
+                     int* err, uint64_t* tl, cudaStream_t st);
 
 // every rank raises its barrier flag on every peer, then waits (bounded) for all
 void launch_rank_barrier(const PeerPtrs& peers, int world, int rank, uint32_t* bar_seq,
@@ -133,7 +141,8 @@ void launch_wait_flags(const uint32_t* flags_local, int first, int world, const 
                        cudaStream_t st);
 
 void launch_combine(int dtype, int64_t n, int topk, int hidden, int world,
-                    const void* yk_local, const void* topk_gate, const uint8_t* valid,
+                    const void* ret_local, const int32_t* ent_ret, const void* topk_gate,
+                    const uint8_t* valid,
                     const void* h, float residual_multiplier, void* out, void* h_out,
                     const uint32_t* flags_local, const uint32_t* seq, WaitCfg wc, int num_sms,
                     uint64_t* tl, cudaStream_t st);
@@ -144,7 +153,7 @@ struct FfnArgs {
   int hidden, inter, world, rank;
   int64_t cap_rows;
   const void* recv_x;       // (cap_rows, H)  local receive buffer
-  const int32_t* recv_meta; // (cap_rows,)    (src << 24) | entry
+  int64_t ret_rows;         // rows of every rank's return buffer (max_tokens * topk)
   void* act;                // (cap_rows, I)  SwiGLU activations
   const void* w_in;         // (E_l, 2I, H)
   const void* w_out;        // (E_l, H, I)

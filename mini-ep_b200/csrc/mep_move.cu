@@ -40,6 +40,31 @@ __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const P
   }
 }
 
+// Entry f (a token's slot): its destination rank my_d and row my_pos in that
+// rank's receive buffer (my_d = -1: not routed, or the destination would
+// overflow, which the layout pass reported), its tag (source rank, entry)
+// stored at the destination, and its row in this rank's return buffer,
+// written back over ent_grp[f] (-1 when not routed) for the combine.
+__device__ __forceinline__ void resolve_slot(int64_t f, int rank, const int64_t* topk_idx,
+                                             const int32_t* ent_dest, int32_t* ent_grp,
+                                             const Layout* lay, const PeerPtrs& peers, int& my_d,
+                                             int64_t& my_pos) {
+  const int d = ent_dest[f];
+  int ret_row = -1;
+  if (d >= 0) {
+    const int e = (int)topk_idx[f];
+    const int off = lay->dst_off[d * kMaxExperts + e];
+    if (off >= 0) {
+      const int grp = ent_grp[f];
+      my_d = d;
+      my_pos = (int64_t)off + grp;
+      peers.recv_meta[d][my_pos] = (rank << 24) | (int32_t)f;
+      ret_row = lay->ret_off[d * kMaxExperts + e] + grp;
+    }
+  }
+  ent_grp[f] = ret_row;
+}
+
 // Dispatch, one warp per token: lanes s < k resolve slot s's destination row
 // in the destination's expert-grouped layout and store the 4-byte tag there
 // (source rank, flat entry index). The warp loads the token's row into one of
@@ -57,7 +82,7 @@ constexpr int kDispatchBufs = 3;  // row buffers per warp
 __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
     int64_t n, int topk, int row_bytes, int world, int rank, int64_t max_tokens,
     const uint8_t* __restrict__ x, const int64_t* __restrict__ topk_idx,
-    const int32_t* __restrict__ ent_dest, const int32_t* __restrict__ ent_grp,
+    const int32_t* __restrict__ ent_dest, int32_t* __restrict__ ent_grp,
     const Layout* __restrict__ lay, PeerPtrs peers, unsigned int* done_ctr, const uint32_t* seq,
     uint64_t* tl) {
   extern __shared__ __align__(128) uint8_t dsmem[];
@@ -70,18 +95,8 @@ __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
   for (int64_t t = (int64_t)blockIdx.x * kDispatchWarps + wp; t < n; t += stride) {
     int my_d = -1;
     int64_t my_pos = 0;
-    if (lane < topk) {
-      const int64_t f = t * topk + lane;
-      const int d = ent_dest[f];
-      if (d >= 0) {
-        const int off = lay->dst_off[d * kMaxExperts + (int)topk_idx[f]];
-        if (off >= 0) {  // a negative offset: the destination would overflow (error raised)
-          my_d = d;
-          my_pos = (int64_t)off + ent_grp[f];
-          peers.recv_meta[d][my_pos] = (rank << 24) | (int32_t)f;
-        }
-      }
-    }
+    if (lane < topk)
+      resolve_slot(t * topk + lane, rank, topk_idx, ent_dest, ent_grp, lay, peers, my_d, my_pos);
     // local slots each need their own row; a remote rank needs the row once
     bool first_remote = my_d >= 0 && my_d != rank;
     for (int j = 0; j < topk; ++j) {
@@ -120,6 +135,142 @@ __global__ void __launch_bounds__(32 * kDispatchWarps) k_dispatch(
   if (lane == 0) {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
+  grid_done_signal(done_ctr, peers, world, rank, world, seq);
+  tl_end(tl, kTlDispatch + 1);
+}
+
+// Dispatch as a streaming engine, one CTA per SM over a contiguous token
+// range. Warp 0 (one lane) bulk-loads the CTA's token rows, in order, into a
+// ring of shared-memory slots (cp.async.bulk global -> shared, completing on
+// the slot's `full` mbarrier). Warps 1.. take the tokens round-robin: lanes
+// s < k resolve slot s's destination and store its tag (as k_dispatch does),
+// then lane 0 waits for the row and issues its bulk copies shared -> global
+// (each local slot's receive row, one landing row per distinct remote rank)
+// as one bulk group. A placing warp keeps kDspPending groups in flight and
+// releases a ring slot (its `empty` mbarrier) once that slot's copies have
+// read shared memory, so the HBM reads, the local writes and the NVLink
+// writes of many tokens overlap. Every wait is bounded.
+// Progress: the loader can wait for a slot that a placing warp still holds
+// only while the ring holds fewer than (placing warps) x (groups in flight
+// - 1) slots, so the host sizes the groups in flight to the ring
+// (dispatch_pending, at most kDspPending).
+constexpr int kDspWarps = 8;      // warp 0 loads, warps 1..7 place
+constexpr int kDspPending = 4;    // bulk groups a placing warp keeps in flight, at most
+constexpr int kDspMaxSlots = 64;  // ring slots (fewer when the rows are long)
+constexpr unsigned long long kDspWaitNs = 2000000000ull;
+
+__device__ __forceinline__ void bulk_wait_read_pending(int keep) {
+  switch (keep) {  // wait_group.read takes an immediate
+    case 0: asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory"); break;
+    default: asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory"); break;
+  }
+}
+
+__global__ void __launch_bounds__(32 * kDspWarps, 1) k_dispatch_stream(
+    int64_t n, int topk, int row_bytes, int world, int rank, int64_t max_tokens, int nslots,
+    int pending, const uint8_t* __restrict__ x, const int64_t* __restrict__ topk_idx,
+    const int32_t* __restrict__ ent_dest, int32_t* __restrict__ ent_grp,
+    const Layout* __restrict__ lay, PeerPtrs peers, unsigned int* done_ctr, const uint32_t* seq,
+    int* err, uint64_t* tl) {
+  extern __shared__ __align__(128) uint8_t dsmem[];
+  __shared__ uint64_t full[kDspMaxSlots], empty[kDspMaxSlots];
+  __shared__ int pend_slot[kDspWarps][kDspPending];
+  __shared__ int abort_flag;
+  const int lane = lane_id(), wp = warp_id();
+  tl_begin(tl, kTlDispatch);
+  const int64_t per = (n + gridDim.x - 1) / gridDim.x;
+  const int64_t t0 = min((int64_t)blockIdx.x * per, n);
+  const int64_t cnt = min(t0 + per, n) - t0;
+  if (threadIdx.x == 0) {
+    for (int sl = 0; sl < nslots; ++sl) {
+      mbar_init(&full[sl], 1);
+      mbar_init(&empty[sl], 1);
+    }
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (wp == 0) {
+    if (lane == 0) {
+      int64_t issued = 0;
+      for (int64_t i = 0; i < cnt; ++i) {
+        const int sl = (int)(i % nslots);
+        const uint32_t ph = (uint32_t)(i / nslots) & 1u;
+        if (!mbar_wait_for(&empty[sl], ph ^ 1u, kDspWaitNs, &abort_flag)) {
+          set_err(err, kErrPipeline);
+          break;
+        }
+        mbar_expect_tx(&full[sl], (uint32_t)row_bytes);
+        bulk_load_g2s(dsmem + (size_t)sl * row_bytes, x + (t0 + i) * (int64_t)row_bytes,
+                      (uint32_t)row_bytes, &full[sl]);
+        issued = i + 1;
+      }
+      // no load may still be writing shared memory when the CTA exits (after
+      // an abort the placing warps did not wait for every row): wait, bounded,
+      // for the last load issued into each slot
+      for (int sl = 0; sl < nslots && sl < issued; ++sl) {
+        const int64_t last = sl + (issued - 1 - sl) / nslots * nslots;
+        mbar_wait_for(&full[sl], (uint32_t)(last / nslots) & 1u, kDspWaitNs, nullptr);
+      }
+    }
+  } else {
+    int pend = 0, head = 0;  // lane 0: groups issued and not yet known read
+    for (int64_t i = wp - 1; i < cnt; i += kDspWarps - 1) {
+      const int64_t t = t0 + i;
+      const int sl = (int)(i % nslots);
+      const uint32_t ph = (uint32_t)(i / nslots) & 1u;
+      int my_d = -1;
+      int64_t my_pos = 0;
+      if (lane < topk)
+        resolve_slot(t * topk + lane, rank, topk_idx, ent_dest, ent_grp, lay, peers, my_d, my_pos);
+      bool first_remote = my_d >= 0 && my_d != rank;
+      for (int j = 0; j < topk; ++j) {
+        const int dj = __shfl_sync(0xffffffffu, my_d, j);
+        if (j < lane && dj == my_d) first_remote = false;
+      }
+      const unsigned remote = __ballot_sync(0xffffffffu, first_remote);
+      const unsigned local = __ballot_sync(0xffffffffu, my_d == rank);
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_for(&full[sl], ph, kDspWaitNs, &abort_flag);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) set_err(err, kErrPipeline);
+        break;
+      }
+      const uint8_t* row = dsmem + (size_t)sl * row_bytes;
+      for (int s = 0; s < topk; ++s) {
+        const int d = __shfl_sync(0xffffffffu, my_d, s);
+        const int64_t pos = __shfl_sync(0xffffffffu, my_pos, s);
+        if (lane == 0) {
+          if ((local >> s) & 1u)
+            bulk_store_s2g(static_cast<uint8_t*>(peers.recv_x[rank]) + pos * row_bytes, row,
+                           (uint32_t)row_bytes);
+          else if ((remote >> s) & 1u)
+            bulk_store_s2g(static_cast<uint8_t*>(peers.land[d]) +
+                               ((int64_t)rank * max_tokens + t) * row_bytes,
+                           row, (uint32_t)row_bytes);
+        }
+      }
+      if (lane == 0) {
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");  // may be empty
+        pend_slot[wp][(head + pend) % kDspPending] = sl;
+        if (++pend > pending - 1) {
+          // all but the newest pending-1 groups have read shared memory
+          bulk_wait_read_pending(pending - 1);
+          mbar_arrive(&empty[pend_slot[wp][head]]);
+          head = (head + 1) % kDspPending;
+          --pend;
+        }
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every copy written
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
   }
   grid_done_signal(done_ctr, peers, world, rank, world, seq);
   tl_end(tl, kTlDispatch + 1);
@@ -255,7 +406,9 @@ __device__ __forceinline__ void add_gated<bf16>(float (&acc)[8], const uint4& ra
 
 template <typename T, int KMAX>
 __device__ __forceinline__ void combine_body(int64_t n, int topk, int H, int world,
-                                             const T* __restrict__ yk, const T* __restrict__ gate,
+                                             const T* __restrict__ ret,
+                                             const int32_t* __restrict__ ent_ret,
+                                             const T* __restrict__ gate,
                                              const uint8_t* __restrict__ valid,
                                              const T* __restrict__ h, float rm,
                                              T* __restrict__ out, T* __restrict__ h_out,
@@ -271,11 +424,16 @@ __device__ __forceinline__ void combine_body(int64_t n, int topk, int H, int wor
   const int nvec = H / V;
   for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp_id(); t < n; t += warps_total) {
     const bool keep = valid == nullptr || valid[t] != 0;
+    // return row of each slot (-1: the entry was not routed)
+    const int my_row = (keep && lane < topk) ? ent_ret[t * topk + lane] : -1;
     float g[KMAX];
+    int row[KMAX];
 #pragma unroll
-    for (int s = 0; s < KMAX; ++s)
-      g[s] = (keep && s < topk) ? Elt<T>::to_f(gate[t * topk + s]) : 0.f;
-    const uint4* rows = reinterpret_cast<const uint4*>(yk + t * topk * (int64_t)H);
+    for (int s = 0; s < KMAX; ++s) {
+      row[s] = __shfl_sync(0xffffffffu, my_row, s < topk ? s : 0);
+      g[s] = (keep && s < topk && row[s] >= 0) ? Elt<T>::to_f(gate[t * topk + s]) : 0.f;
+    }
+    const uint4* rows = reinterpret_cast<const uint4*>(ret);
     for (int c = lane; c < nvec; c += 32) {
       float acc[V];
 #pragma unroll
@@ -288,7 +446,8 @@ __device__ __forceinline__ void combine_body(int64_t n, int topk, int H, int wor
         uint4 raw[KMAX];
 #pragma unroll
         for (int s = 0; s < KMAX; ++s)
-          if (s < topk) raw[s] = rows[(int64_t)s * nvec + c];
+          raw[s] = (s < topk && row[s] >= 0) ? rows[(int64_t)row[s] * nvec + c]
+                                             : make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int s = 0; s < KMAX; ++s) {
           if (s < topk) add_gated<T>(acc, raw[s], g[s]);
@@ -316,36 +475,61 @@ __device__ __forceinline__ void combine_body(int64_t n, int topk, int H, int wor
 // compiler's own register choice, its slot array needs them
 template <typename T>
 __global__ void __launch_bounds__(256, 3) k_combine8(int64_t n, int topk, int H, int world,
-                                                     const T* __restrict__ yk,
+                                                     const T* __restrict__ ret,
+                                                     const int32_t* __restrict__ ent_ret,
                                                      const T* __restrict__ gate,
                                                      const uint8_t* __restrict__ valid,
                                                      const T* __restrict__ h, float rm,
                                                      T* __restrict__ out, T* __restrict__ h_out,
                                                      const uint32_t* flags, const uint32_t* seq,
                                                      WaitCfg wc, uint64_t* tl) {
-  combine_body<T, 8>(n, topk, H, world, yk, gate, valid, h, rm, out, h_out, flags, seq, wc, tl);
+  combine_body<T, 8>(n, topk, H, world, ret, ent_ret, gate, valid, h, rm, out, h_out, flags, seq,
+                     wc, tl);
 }
 template <typename T>
 __global__ void __launch_bounds__(256) k_combine16(int64_t n, int topk, int H, int world,
-                                                   const T* __restrict__ yk,
+                                                   const T* __restrict__ ret,
+                                                   const int32_t* __restrict__ ent_ret,
                                                    const T* __restrict__ gate,
                                                    const uint8_t* __restrict__ valid,
                                                    const T* __restrict__ h, float rm,
                                                    T* __restrict__ out, T* __restrict__ h_out,
                                                    const uint32_t* flags, const uint32_t* seq,
                                                    WaitCfg wc, uint64_t* tl) {
-  combine_body<T, kMaxTopk>(n, topk, H, world, yk, gate, valid, h, rm, out, h_out, flags, seq,
-                            wc, tl);
+  combine_body<T, kMaxTopk>(n, topk, H, world, ret, ent_ret, gate, valid, h, rm, out, h_out,
+                            flags, seq, wc, tl);
 }
 
 }  // namespace
 
 void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int rank,
                      int64_t max_tokens, const void* x, const int64_t* topk_idx,
-                     const int32_t* ent_dest, const int32_t* ent_grp, const Layout* layout,
+                     const int32_t* ent_dest, int32_t* ent_grp, const Layout* layout,
                      const PeerPtrs& peers, unsigned int* done_ctr, const uint32_t* seq,
-                     int num_sms, uint64_t* tl, cudaStream_t st) {
+                     int num_sms, int per_warp, int* err, uint64_t* tl, cudaStream_t st) {
   const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
+  if (!per_warp) {
+    // ring slots within ~200 KB of dynamic shared memory
+    int nslots = (200 * 1024) / row_bytes;
+    if (nslots > kDspMaxSlots) nslots = kDspMaxSlots;
+    if (nslots < 2) nslots = 2;
+    const size_t smem = (size_t)nslots * row_bytes;
+    static size_t stream_smem_set = 0;
+    if (smem > 48 * 1024 && smem > stream_smem_set) {
+      cudaFuncSetAttribute(k_dispatch_stream, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+      stream_smem_set = smem;
+    }
+    // groups in flight per placing warp: the ring must hold more than
+    // (placing warps) x (pending - 1) slots (see kDspWarps)
+    int pending = (nslots - 1) / (kDspWarps - 1) + 1;
+    if (pending > kDspPending) pending = kDspPending;
+    k_dispatch_stream<<<(unsigned)num_sms, 32 * kDspWarps, smem, st>>>(
+        n, topk, row_bytes, world, rank, max_tokens, nslots, pending,
+        static_cast<const uint8_t*>(x),
+        topk_idx, ent_dest, ent_grp, layout, peers, done_ctr, seq, err, tl);
+    return;
+  }
   const size_t smem = (size_t)kDispatchWarps * kDispatchBufs * row_bytes;
   static size_t smem_set = 0;
   if (smem > 48 * 1024 && smem > smem_set) {
@@ -381,8 +565,8 @@ void launch_wait_flags(const uint32_t* flags_local, int first, int world, const 
   k_wait_flags<<<1, 32, 0, st>>>(flags_local, first, world, seq, target, errcode, wc, tl, tl_slot);
 }
 
-void launch_combine(int dtype, int64_t n, int topk, int hidden, int world, const void* yk_local,
-                    const void* topk_gate, const uint8_t* valid, const void* h,
+void launch_combine(int dtype, int64_t n, int topk, int hidden, int world, const void* ret_local,
+                    const int32_t* ent_ret, const void* topk_gate, const uint8_t* valid, const void* h,
                     float residual_multiplier, void* out, void* h_out, const uint32_t* flags_local,
                     const uint32_t* seq, WaitCfg wc, int num_sms, uint64_t* tl, cudaStream_t st) {
   int64_t blocks = (n + 7) / 8;
@@ -391,7 +575,8 @@ void launch_combine(int dtype, int64_t n, int topk, int hidden, int world, const
   // slot rows in flight per lane: sized to top-k (8 or 16) to keep registers low
 #define MEP_COMBINE(T, KM)                                                                  \
   k_combine##KM<T><<<(unsigned)blocks, 256, 0, st>>>(                                       \
-      n, topk, hidden, world, static_cast<const T*>(yk_local), static_cast<const T*>(topk_gate), \
+      n, topk, hidden, world, static_cast<const T*>(ret_local), ent_ret,                       \
+      static_cast<const T*>(topk_gate),                                                       \
       valid, static_cast<const T*>(h), residual_multiplier, static_cast<T*>(out),             \
       static_cast<T*>(h_out), flags_local, seq, wc, tl)
   static_assert(kMaxTopk == 16, "combine kernels are instantiated for top-8 and top-16");

@@ -152,25 +152,51 @@ __global__ void __launch_bounds__(256) k_route_rr_advance(int nchunks, int E,
   }
 }
 
-// Receive layout + send offsets from the exchanged counts C[s][d][e], by one
-// CTA, once every rank's counts for step `step` have arrived (bounded wait).
+__device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+// Receive layout, send offsets and return-buffer tables from the exchanged
+// counts C[s][d][e], by one CTA (256 threads), once every rank's counts for
+// step `step` have arrived (bounded wait). Csm: world * world * E ints of
+// shared memory for C.
+//   receive side (this rank as owner d = rank): expert segments in
+//     increasing expert order, each padded to kRowAlign rows, sources in rank
+//     order inside a segment;
+//   send side: dst_off[d][e] = the row of rank d's segment of e where this
+//     rank's rows start;
+//   return side: this rank's expert outputs come back in (owner d, expert e,
+//     group index) order, group (d, e) starting at ret_off[d][e]; as an owner,
+//     segment j's rows from source s start at src_begin[j][s] inside the
+//     segment and belong at row ret_row[j][s] of s's return buffer.
 __device__ void layout_block(int world, int rank, int E, const int32_t* __restrict__ owners,
                              const int32_t* __restrict__ nrep, const int32_t* cnt_in,
                              const uint32_t* flags, int64_t* __restrict__ recv_per_layer,
                              int64_t cap_rows, Layout* __restrict__ lay, uint32_t step,
-                             const WaitCfg& wc) {
+                             const WaitCfg& wc, int* Csm) {
   __shared__ int R[kMaxWorld][kMaxExperts];       // rows per (dest, expert)
   __shared__ int before[kMaxWorld][kMaxExperts];  // rows from sources < rank
   __shared__ int seg[kMaxWorld][kMaxExperts];
   __shared__ unsigned char res[kMaxWorld][kMaxExperts];
+  __shared__ int jof[kMaxExperts];                // local segment of expert e, or -1
   __shared__ int overflow[kMaxWorld];
+  const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int WE = world * E;
   if (threadIdx.x < world) wait_flag(flags + threadIdx.x, step, kErrWaitCounts, wc);
   __syncthreads();
-  for (int i = threadIdx.x; i < world * E; i += blockDim.x) {
+  // peers stored the counts over NVLink: read them at L2 (not a stale L1 line)
+  for (int i = threadIdx.x; i < world * WE; i += blockDim.x) Csm[i] = __ldcg(cnt_in + i);
+  __syncthreads();
+  for (int i = threadIdx.x; i < WE; i += blockDim.x) {
     const int d = i / E, e = i % E;
     int tot = 0, bef = 0;
     for (int s = 0; s < world; ++s) {
-      const int c = __ldcv(cnt_in + ((int64_t)s * world + d) * E + e);
+      const int c = Csm[s * WE + i];
       tot += c;
       if (s < rank) bef += c;
     }
@@ -182,41 +208,94 @@ __device__ void layout_block(int world, int rank, int E, const int32_t* __restri
     if (tot > 0 && !r) set_err(wc.err, kErrNotResident);
   }
   __syncthreads();
-  if (threadIdx.x < world) {
-    const int d = threadIdx.x;
-    int64_t b = 0;
-    for (int e = 0; e < E; ++e) {
-      seg[d][e] = (int)b;
-      if (res[d][e]) b += (R[d][e] + kRowAlign - 1) / kRowAlign * kRowAlign;
+  // warp d: padded segment bases at destination d (a scan over experts)
+  if (wp < world) {
+    const int d = wp;
+    int run = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int v = (e < E && res[d][e]) ? (R[d][e] + kRowAlign - 1) / kRowAlign * kRowAlign : 0;
+      const int inc = warp_inclusive_scan(v, lane);
+      if (e < E) seg[d][e] = run + inc - v;
+      run += __shfl_sync(0xffffffffu, inc, 31);
     }
-    overflow[d] = b > cap_rows;
-    if (b > cap_rows) set_err(wc.err, kErrCapacity);
+    if (lane == 0) {
+      overflow[d] = run > cap_rows;
+      if (run > cap_rows) set_err(wc.err, kErrCapacity);
+    }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < world * E; i += blockDim.x) {
+  for (int i = threadIdx.x; i < WE; i += blockDim.x) {
     const int d = i / E, e = i % E;
     lay->dst_off[d * kMaxExperts + e] = overflow[d] ? -1 : seg[d][e] + before[d][e];
   }
-  if (threadIdx.x == 0) {
-    int j = 0, tiles = 0, rows = 0, end = 0;
-    for (int e = 0; e < E; ++e) {
-      if (!res[rank][e]) continue;
-      lay->local_expert[j] = e;
-      lay->seg_base[j] = seg[rank][e];
-      lay->seg_rows[j] = R[rank][e];
-      lay->tile_prefix[j] = tiles;
-      const int t = (R[rank][e] + kRowAlign - 1) / kRowAlign;
-      tiles += t;
-      rows += R[rank][e];
-      end = seg[rank][e] + t * kRowAlign;
-      ++j;
+  // warp 0: this rank's local segments (scans over the resident experts)
+  if (wp == 0) {
+    int jrun = 0, trun = 0, rows = 0, end = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int mine = e < E && res[rank][e];
+      const int rws = mine ? R[rank][e] : 0;
+      const int t = (rws + kRowAlign - 1) / kRowAlign;
+      const int jin = warp_inclusive_scan(mine, lane);
+      const int tin = warp_inclusive_scan(t, lane);
+      const int rin = warp_inclusive_scan(rws, lane);
+      if (e < E) jof[e] = mine ? jrun + jin - 1 : -1;
+      if (mine) {
+        const int j = jrun + jin - 1;
+        lay->local_expert[j] = e;
+        lay->seg_base[j] = seg[rank][e];
+        lay->seg_rows[j] = rws;
+        lay->tile_prefix[j] = trun + tin - t;
+        end = seg[rank][e] + t * kRowAlign;  // the last resident expert's lane holds the end
+      }
+      jrun += __shfl_sync(0xffffffffu, jin, 31);
+      trun += __shfl_sync(0xffffffffu, tin, 31);
+      rows += __shfl_sync(0xffffffffu, rin, 31);
+      // the end of the last segment so far: the highest lane that holds one
+      const unsigned has = __ballot_sync(0xffffffffu, mine);
+      if (has) end = __shfl_sync(0xffffffffu, end, 31 - __clz(has));
     }
-    lay->tile_prefix[j] = tiles;
-    lay->n_local = j;
-    lay->total_mtiles = overflow[rank] ? 0 : tiles;
-    lay->total_rows = end;
-    lay->recv_rows = rows;
-    if (recv_per_layer) recv_per_layer[0] += rows;
+    if (lane == 0) {
+      lay->tile_prefix[jrun] = trun;
+      lay->n_local = jrun;
+      lay->total_mtiles = overflow[rank] ? 0 : trun;
+      lay->total_rows = end;
+      lay->recv_rows = rows;
+      if (recv_per_layer) recv_per_layer[0] += rows;
+    }
+  }
+  __syncthreads();
+  // warp s: running row offset of source s's return buffer over (owner d,
+  // expert e) in order; its own buffer's group starts (s == rank), and where
+  // the rows it sent this rank go (d == rank)
+  if (wp < world) {
+    const int src = wp;
+    int run = 0;
+    for (int d = 0; d < world; ++d) {
+      for (int e0 = 0; e0 < E; e0 += 32) {
+        const int e = e0 + lane;
+        const int v = e < E ? Csm[src * WE + d * E + e] : 0;
+        const int inc = warp_inclusive_scan(v, lane);
+        const int excl = run + inc - v;
+        if (e < E) {
+          if (src == rank) lay->ret_off[d * kMaxExperts + e] = excl;
+          if (d == rank && jof[e] >= 0) lay->ret_row[jof[e] * kMaxWorld + src] = excl;
+        }
+        run += __shfl_sync(0xffffffffu, inc, 31);
+      }
+    }
+  }
+  // per local segment: where each source's rows start inside it
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int j = jof[e];
+    if (j < 0) continue;
+    int run = 0;
+    for (int src = 0; src < world; ++src) {
+      lay->src_begin[j * (kMaxWorld + 1) + src] = run;
+      run += Csm[src * WE + rank * E + e];
+    }
+    lay->src_begin[j * (kMaxWorld + 1) + world] = run;
   }
 }
 
@@ -364,8 +443,9 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
       tl_mark(tl, kTlCountsSent);
     }
     // the receive layout, once every rank's counts are in (the other CTAs rank meanwhile)
+    extern __shared__ int route_dyn[];  // world * world * E counts for the layout pass
     layout_block(world, rank, E, owners, nrep, cnt_in, flags, recv_per_layer, cap_rows, lay, step,
-                 wc);
+                 wc, route_dyn);
     __syncthreads();
     if (threadIdx.x == 0) tl_mark(tl, kTlLayout);
   }
@@ -443,7 +523,13 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
   int64_t grid = rounds < num_sms ? rounds : num_sms;
   if (grid < 1) grid = 1;
   const int64_t tpc = (rounds + grid - 1) / grid * kRouteChunkTokens;
-  k_route_fused<<<(unsigned)grid, kRouteThreads, 0, st>>>(
+  const size_t dyn = (size_t)world * world * experts * sizeof(int);  // <= 32 KiB
+  static size_t dyn_set = 0;
+  if (dyn > dyn_set) {
+    cudaFuncSetAttribute(k_route_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+    dyn_set = dyn;
+  }
+  k_route_fused<<<(unsigned)grid, kRouteThreads, dyn, st>>>(
       n, topk, experts, tpc, world, rank, topk_idx, valid, owners_l, nrep_l, rr_l, route_counts_l,
       chunk_hist, ent_dest, ent_grp, my_counts, peers, seq, reinterpret_cast<RouteSync*>(sync),
       cnt_in_local, flags_local, recv_per_layer_l, cap_rows, layout, wc, tl);
