@@ -44,6 +44,7 @@ struct mep_ctx {
   int force_simt = 0;
   int tc_single_cta = 0;
   int dispatch_per_warp = 0;  // 1: one warp per token (k_dispatch) instead of the streaming engine
+  int router_no_tc = 0;       // 1: never the tcgen05 router
   std::vector<int> placed, n_local_l;
   int cur_layer = -1, stage = 0;
   int64_t cur_n = 0;
@@ -348,7 +349,7 @@ int mep_router_topk(mep_ctx* c, const void* x, const void* router_w, const float
     return fail(c, MEP_ERR_INVALID, "NULL argument");
   if (int rc = use_device(c)) return rc;
   launch_router(c->dtype, x, router_w, bias, n, c->H, c->E, c->k, topk_idx_out, topk_gate_out,
-                logits_out, c->num_sms, c->err_dev, tl_of(c), as_stream(stream));
+                logits_out, c->num_sms, !c->router_no_tc, c->err_dev, tl_of(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   return MEP_OK;
 }
@@ -582,6 +583,10 @@ int mep_set_option(mep_ctx* c, const char* name, int64_t value) {
   }
   if (!std::strcmp(name, "tc_single_cta")) {
     c->tc_single_cta = value != 0;
+    return MEP_OK;
+  }
+  if (!std::strcmp(name, "router_no_tc")) {
+    c->router_no_tc = value != 0;
     return MEP_OK;
   }
   if (!std::strcmp(name, "dispatch_per_warp")) {

@@ -24,6 +24,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include "mep_device.cuh"
+#include "mep_tc.cuh"
 
 namespace mep {
 namespace {
@@ -175,7 +176,8 @@ __global__ void __launch_bounds__(256) k_ffn_simt(const T* __restrict__ A, int l
 }
 
 // =================================================================== tcgen05
-namespace tc {
+namespace ffn {
+using namespace ::mep::tc;  // the shared tcgen05 / TMA building blocks (mep_tc.cuh)
 constexpr int BN = 256, BK = 64;
 constexpr int A_TILE = 128 * BK * 2;            // 16 KiB: 128 rows x 64 bf16 (one 128B-swizzle row each)
 constexpr int EPI_WARPS = 8;                    // two per TMEM lane quadrant, splitting the columns
@@ -238,124 +240,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, Smem<PAI
       }
     }
   }
-}
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// shared::cluster address of the same location in CTA `cta` of this cluster
-__device__ __forceinline__ uint32_t map_to_cta(const void* p, uint32_t cta) {
-  uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(cta));
-  return out;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// 2D TMA tile load into this CTA's shared memory. Single CTA: completes on
-// this CTA's barrier. Pair: completes on the pair leader's barrier, given as
-// a shared::cluster address.
-template <bool PAIR>
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y,
-                                            uint32_t bar) {
-  if (PAIR)
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-  else
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-// 2D TMA tile store from this CTA's shared memory (128B-swizzled rows), in
-// the issuing thread's bulk group
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::
-                   "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(src))
-               : "memory");
-}
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: 8 rows x 128 B
-  d |= (uint64_t)1 << 46;             // descriptor version for tcgen05
-  d |= (uint64_t)2 << 61;             // 128-byte swizzle
-  return d;
-}
-template <bool PAIR>
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                        uint32_t accumulate) {
-  if (PAIR)
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-  else
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-}
-// completion of this thread's prior MMAs arrives on `bar` (pair: on the
-// barrier at the same offset in both CTAs)
-template <bool PAIR>
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  if (PAIR) {
-    const uint16_t both = 0x3;
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%0], %1;" ::"r"(smem_u32(bar)),
-        "h"(both)
-        : "memory");
-  } else {
-    asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-            smem_u32(bar))
-        : "memory");
-  }
-}
-// "accumulator drained" arrival: relaxed, because it only releases TMEM
-// (ordered by tcgen05.fence::before_thread_sync), not the epilogue's global
-// stores, which must not be waited for here
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
-               : "memory");
-}
-__device__ __forceinline__ void fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&p);
-}
-__device__ __forceinline__ float bf16_round(float v) {
-  return __bfloat162float(__float2bfloat16_rn(v));
 }
 // silu(bf16(g)) rounded to bf16, times bf16(u): the rounding points of the
 // reference's bf16 SwiGLU (modeling.py:102-103). The fp32 sigmoid uses the
@@ -710,41 +594,49 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
               uint32_t box_outer) {
+  return encode_bf16_2d(m, base, inner, outer, BK, box_outer);
+}
+
+}  // namespace ffn
+}  // namespace
+
+// bf16 2D tensor map (rows of `inner` elements, `outer` rows), box
+// box_inner x box_outer, 128-byte swizzle
+int encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
+                   uint32_t box_inner, uint32_t box_outer) {
+  if (int rc = tc_init()) return rc;
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {inner * 2};
-  const cuuint32_t box[2] = {BK, box_outer};
+  const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t es[2] = {1, 1};
-  const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                              strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = ffn::g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                                  dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -100 - (int)r;
 }
 
-}  // namespace tc
-}  // namespace
-
 bool tc_shape_ok(int hidden, int inter) {
-  return hidden % tc::BN == 0 && inter % 128 == 0;
+  return hidden % ffn::BN == 0 && inter % 128 == 0;
 }
 
 int tc_init() {
-  if (tc::g_encode) return 0;
+  if (ffn::g_encode) return 0;
   void* fn = nullptr;
   cudaDriverEntryPointQueryResult q;
   const cudaError_t e =
       cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
   if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return -1;
-  if (cudaFuncSetAttribute(tc::k_ffn_tc<0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::smem_bytes<false>()) != cudaSuccess ||
-      cudaFuncSetAttribute(tc::k_ffn_tc<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::smem_bytes<false>()) != cudaSuccess ||
-      cudaFuncSetAttribute(tc::k_ffn_tc<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::smem_bytes<true>()) != cudaSuccess ||
-      cudaFuncSetAttribute(tc::k_ffn_tc<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           tc::smem_bytes<true>()) != cudaSuccess)
+  if (cudaFuncSetAttribute(ffn::k_ffn_tc<0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           ffn::smem_bytes<false>()) != cudaSuccess ||
+      cudaFuncSetAttribute(ffn::k_ffn_tc<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           ffn::smem_bytes<false>()) != cudaSuccess ||
+      cudaFuncSetAttribute(ffn::k_ffn_tc<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           ffn::smem_bytes<true>()) != cudaSuccess ||
+      cudaFuncSetAttribute(ffn::k_ffn_tc<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           ffn::smem_bytes<true>()) != cudaSuccess)
     return -2;
-  tc::g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  ffn::g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   return 0;
 }
 
@@ -756,11 +648,11 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     if (rc) return rc;
     CUtensorMap tmA1, tmB1, tmA2, tmB2;
     const uint64_t nl = (uint64_t)(a.n_local_weights > 0 ? a.n_local_weights : 1);
-    if ((rc = tc::make_tmap(&tmA1, a.recv_x, H, a.cap_rows, 128))) return rc;
-    if ((rc = tc::make_tmap(&tmA2, a.act, I, a.cap_rows, 128))) return rc;
-    if ((rc = tc::make_tmap(&tmB1, a.w_in, H, nl * 2 * I, 128))) return rc;
-    if ((rc = tc::make_tmap(&tmB2, a.w_out, I, nl * H, 128))) return rc;
-    tc::TcArgs g1{};
+    if ((rc = ffn::make_tmap(&tmA1, a.recv_x, H, a.cap_rows, 128))) return rc;
+    if ((rc = ffn::make_tmap(&tmA2, a.act, I, a.cap_rows, 128))) return rc;
+    if ((rc = ffn::make_tmap(&tmB1, a.w_in, H, nl * 2 * I, 128))) return rc;
+    if ((rc = ffn::make_tmap(&tmB2, a.w_out, I, nl * H, 128))) return rc;
+    ffn::TcArgs g1{};
     g1.lay = a.layout;
     g1.K = H;
     g1.ntiles_n = I / 128;
@@ -774,17 +666,17 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     const bool pair = !a.tc_single_cta && a.num_sms >= 2;
     // CTA pairs: 2-CTA clusters over an even grid; single CTAs: one per SM
     // GEMM2's tile stores: every rank's return buffer (ranks past world: unused)
-    tc::RetMaps rmaps;
+    ffn::RetMaps rmaps;
     std::memset(&rmaps, 0, sizeof(rmaps));
     for (int r = 0; r < a.world; ++r)
-      if ((rc = tc::make_tmap(&rmaps.m[r], a.peers.ret[r], H, (uint64_t)a.ret_rows, 32)))
+      if ((rc = ffn::make_tmap(&rmaps.m[r], a.peers.ret[r], H, (uint64_t)a.ret_rows, 32)))
         return rc;
     auto launch = [&](auto kernel, bool as_pair, const CUtensorMap& ta, const CUtensorMap& tb,
-                      const tc::TcArgs& g) -> cudaError_t {
+                      const ffn::TcArgs& g) -> cudaError_t {
       cudaLaunchConfig_t cfg{};
       cfg.gridDim = dim3((unsigned)(as_pair ? (a.num_sms & ~1) : a.num_sms));
-      cfg.blockDim = dim3(tc::THREADS);
-      cfg.dynamicSmemBytes = as_pair ? tc::smem_bytes<true>() : tc::smem_bytes<false>();
+      cfg.blockDim = dim3(ffn::THREADS);
+      cfg.dynamicSmemBytes = as_pair ? ffn::smem_bytes<true>() : ffn::smem_bytes<false>();
       cfg.stream = st;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -795,15 +687,15 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
       cfg.numAttrs = as_pair ? 1 : 0;
       return cudaLaunchKernelEx(&cfg, kernel, ta, tb, rmaps, g);
     };
-    cudaError_t e = pair ? launch(tc::k_ffn_tc<0, true>, true, tmA1, tmB1, g1)
-                         : launch(tc::k_ffn_tc<0, false>, false, tmA1, tmB1, g1);
+    cudaError_t e = pair ? launch(ffn::k_ffn_tc<0, true>, true, tmA1, tmB1, g1)
+                         : launch(ffn::k_ffn_tc<0, false>, false, tmA1, tmB1, g1);
     if (e != cudaSuccess) return (int)e;
-    tc::TcArgs g2{};
+    ffn::TcArgs g2{};
     g2.lay = a.layout;
     g2.K = I;
-    g2.ntiles_n = H / tc::BN;
+    g2.ntiles_n = H / ffn::BN;
     g2.b_rows_per_expert = H;
-    g2.b_step = tc::BN;
+    g2.b_step = ffn::BN;
     g2.b_second = 128;
     g2.peers = a.peers;
     g2.H = H;
@@ -813,8 +705,8 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g2.seq = a.seq;
     g2.err = a.err;
     g2.tl = a.tl;
-    e = pair ? launch(tc::k_ffn_tc<1, true>, true, tmA2, tmB2, g2)
-             : launch(tc::k_ffn_tc<1, false>, false, tmA2, tmB2, g2);
+    e = pair ? launch(ffn::k_ffn_tc<1, true>, true, tmA2, tmB2, g2)
+             : launch(ffn::k_ffn_tc<1, false>, false, tmA2, tmB2, g2);
     if (e != cudaSuccess) return (int)e;
     return (int)cudaGetLastError();
   }

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
@@ -90,10 +91,17 @@ struct WaitCfg {
 // ---------------------------------------------------------------- router
 // `tl` (every launcher below that takes it): the step timeline, or null when
 // the context's timeline option is off (mep_device.cuh, tl_begin / tl_end)
+// use_tc: allow the tcgen05 router from kRouterTcMinTokens tokens
+constexpr int64_t kRouterTcMinTokens = 4096;
 void launch_router(int dtype, const void* x, const void* router_w, const float* bias,
                    int64_t n, int hidden, int experts, int topk, int64_t* idx_out,
-                   void* gate_out, float* logits_out, int num_sms, int* err, uint64_t* tl,
-                   cudaStream_t st);
+                   void* gate_out, float* logits_out, int num_sms, int use_tc, int* err,
+                   uint64_t* tl, cudaStream_t st);
+// the tcgen05 router (mep_router_tc.cu): 0 when it ran, nonzero when the
+// shape is not covered (bf16, E of 32 or 64, H a multiple of 64, 16-byte rows)
+int launch_router_tc(int64_t n, int hidden, int experts, int topk, const void* x,
+                     const void* router_w, const float* bias, int64_t* idx_out, void* gate_out,
+                     float* logits_out, int num_sms, int* err, uint64_t* tl, cudaStream_t st);
 
 // ---------------------------------------------------------------- RMSNorm
 void launch_rmsnorm(int dtype, int64_t n, int hidden, const void* h, const void* w, float eps,
@@ -172,5 +180,8 @@ struct FfnArgs {
 int launch_ffn(const FfnArgs& a, cudaStream_t st);
 bool tc_shape_ok(int hidden, int inter);
 int tc_init();  // resolves cuTensorMapEncodeTiled; 0 ok
+// bf16 2D tensor map with 128-byte swizzle (mep_ffn.cu); 0 ok
+int encode_bf16_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
+                   uint32_t box_inner, uint32_t box_outer);
 
 }  // namespace mep

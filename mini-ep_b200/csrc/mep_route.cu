@@ -375,9 +375,14 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     rr_mod[e] = (int)(((rr[e] % nrep[e]) + nrep[e]) % nrep[e]);  // >= 0 for any rr
   }
   __syncthreads();
-  for (int64_t f = t_beg * k + threadIdx.x; f < t_end * k; f += blockDim.x) {
-    const int e = entry_expert(idx, valid, f, k, n, E, wc.err);
-    if (e >= 0) atomicAdd(&hist[e], 1);
+  // lanes holding the same expert add once (skewed routing piles entries on
+  // a few experts, so one shared counter would take most of the atomics)
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int64_t f0 = t_beg * k; f0 < t_end * k; f0 += blockDim.x) {
+    const int64_t f = f0 + threadIdx.x;
+    const int e = f < t_end * k ? entry_expert(idx, valid, f, k, n, E, wc.err) : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && (same & lt_mask) == 0) atomicAdd(&hist[e], __popc(same));
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_hist[(int64_t)b * E + e] = hist[e];
@@ -408,9 +413,10 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   }
   __syncthreads();
 
+  uint32_t step = 0;  // CTA 0: the sequence number of this layer step
   if (b == 0) {
     // finalize: counts per (dest, expert), rr, stats, publish
-    const uint32_t step = *seq + 1u;
+    step = *seq + 1u;
     for (int i = threadIdx.x; i < world * E; i += blockDim.x) cnt[i] = 0;
     for (int e = threadIdx.x; e < E; e += blockDim.x)
       if (nrep[e] > 1) any_rep = 1;
@@ -442,16 +448,9 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
       *seq = step;
       tl_mark(tl, kTlCountsSent);
     }
-    // the receive layout, once every rank's counts are in (the other CTAs rank meanwhile)
-    extern __shared__ int route_dyn[];  // world * world * E counts for the layout pass
-    layout_block(world, rank, E, owners, nrep, cnt_in, flags, recv_per_layer, cap_rows, lay, step,
-                 wc, route_dyn);
-    __syncthreads();
-    if (threadIdx.x == 0) tl_mark(tl, kTlLayout);
   }
 
   // ---- ranking, 256 tokens per round (8 warps x 32 tokens)
-  const unsigned lt_mask = (1u << lane) - 1u;
   for (int64_t r0 = t_beg; r0 < t_end; r0 += kRouteChunkTokens) {
     for (int e = threadIdx.x; e < E; e += blockDim.x)
       for (int w = 0; w < kRouteWarps; ++w) wcnt[w][e] = 0;
@@ -462,7 +461,8 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     for (int r = 0; r < k; ++r) {
       const int64_t f = f0 + r * 32 + lane;
       const int e = f < f_end ? entry_expert(idx, valid, f, k, n, E, nullptr) : -1;
-      if (e >= 0) atomicAdd(&wcnt[wp][e], 1);
+      const unsigned same = __match_any_sync(0xffffffffu, e);
+      if (e >= 0 && (same & lt_mask) == 0) wcnt[wp][e] += __popc(same);
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -499,6 +499,15 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] += hist[e];
     __syncthreads();
+  }
+  if (b == 0) {
+    // the receive layout, once every rank's counts are in: after this CTA's
+    // own ranking, which overlaps the peers' publishing
+    extern __shared__ int route_dyn[];  // world * world * E counts for the layout pass
+    layout_block(world, rank, E, owners, nrep, cnt_in, flags, recv_per_layer, cap_rows, lay,
+                 step, wc, route_dyn);
+    __syncthreads();
+    if (threadIdx.x == 0) tl_mark(tl, kTlLayout);
   }
   tl_end(tl, kTlRoute + 1);
 }

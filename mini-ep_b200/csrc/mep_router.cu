@@ -268,12 +268,17 @@ __global__ void __launch_bounds__(128) k_router_simt(
 
 void launch_router(int dtype, const void* x, const void* router_w, const float* bias, int64_t n,
                    int hidden, int experts, int topk, int64_t* idx_out, void* gate_out,
-                   float* logits_out, int num_sms, int* err, uint64_t* tl, cudaStream_t st) {
-  (void)num_sms;
-  (void)err;
+                   float* logits_out, int num_sms, int use_tc, int* err, uint64_t* tl,
+                   cudaStream_t st) {
   if (n <= 0) return;
-  // the tensor-core kernel reads x and the router rows in 16-byte pieces; the
-  // CUDA-core kernel takes any layout
+  // large batches: the tcgen05 router (TMA-fed, one CTA per SM); it covers
+  // bf16 with 32 or 64 experts and rows on 16-byte boundaries
+  if (dtype == kBF16 && use_tc && n >= kRouterTcMinTokens &&
+      launch_router_tc(n, hidden, experts, topk, x, router_w, bias, idx_out, gate_out,
+                       logits_out, num_sms, err, tl, st) == 0)
+    return;
+  // the warp-level tensor-core kernel reads x and the router rows in 16-byte
+  // pieces; the CUDA-core kernel takes any layout
   const bool aligned16 = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(router_w)) &
                           15u) == 0;
   if (dtype == kBF16 && hidden % 64 == 0 && experts % 8 == 0 && experts <= 64 && aligned16) {

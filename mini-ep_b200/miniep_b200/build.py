@@ -23,8 +23,8 @@ INCLUDE = ROOT.parent / "include"
 LIB = PKG / "libminiep_b200.so"
 OBJ = ROOT / "_build"
 
-SOURCES = ["mep_api.cu", "mep_router.cu", "mep_route.cu", "mep_move.cu", "mep_ffn.cu",
-           "mep_noalloc.cu", "mep_norm.cu"]
+SOURCES = ["mep_api.cu", "mep_router.cu", "mep_router_tc.cu", "mep_route.cu", "mep_move.cu",
+           "mep_ffn.cu", "mep_noalloc.cu", "mep_norm.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr"]
 

@@ -68,7 +68,9 @@ def test_router_fp32_config1(golden):
                           rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("shape,n", [("a", 4096), ("a", 1), ("a", 1000), ("b", 1024), ("b", 33)])
+# 4096 and more tokens take the tcgen05 router, fewer the warp-level kernel
+@pytest.mark.parametrize("shape,n", [("a", 4096), ("a", 1), ("a", 1000), ("b", 1024), ("b", 33),
+                                     ("b", 4100), ("a", 20000)])
 def test_router_bf16_skewed(shape, n):
     sh = synth.SHAPES[shape]
     lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=1, dtype=torch.bfloat16)
@@ -106,6 +108,32 @@ def test_router_bf16_skewed(shape, n):
                        torch.bincount(ref_idx[ok].reshape(-1), minlength=sh["experts"]))
     print(f"router {shape} n={n}: exact-tie rows {int(ties.sum())}, "
           f"rounding-moved rows {int(off.sum())} of {int((~ties).sum())} tie-free")
+
+
+@pytest.mark.parametrize("shape", ["a", "b"])
+def test_router_tcgen05_and_warp_kernels_agree(shape):
+    """The tcgen05 router (large batches) and the warp-level kernel select
+    the same experts and gates wherever their fp32 sums round to the same
+    bf16 logits, and their logits differ by at most one rounding step."""
+    sh = synth.SHAPES[shape]
+    n = 8192
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=5, dtype=torch.bfloat16)
+    bias = synth.zipf_router_bias(1, sh["experts"])[0].cuda()
+    comm = world1_comm(sh["experts"], sh["topk"], sh["hidden"], sh["inter"], n, torch.bfloat16)
+    x, w = lb.x.cuda(), lb.router.cuda()
+    got = {}
+    for no_tc in (0, 1):
+        comm.set_option("router_no_tc", no_tc)
+        got[no_tc] = [t.cpu() for t in router_topk(comm, x, w, bias, return_logits=True)]
+    comm.check()
+    (i_tc, g_tc, l_tc), (i_w, g_w, l_w) = got[0], got[1]
+    ulp = l_w.abs().clamp_min(2.0 ** -20) * 2.0 ** -7
+    assert torch.all((l_tc - l_w).abs() <= ulp)
+    same = (l_tc == l_w).all(dim=1)
+    assert same.float().mean() > 0.9
+    assert torch.equal(i_tc[same], i_w[same])
+    assert torch.equal(g_tc[same], g_w[same])
+    assert torch.equal(i_tc, O.topk_lowest_index(l_tc, sh["topk"]))
 
 
 def test_dispatch_rejects_rows_not_16_byte_aligned():
