@@ -77,11 +77,12 @@ def parse():
     ap.add_argument("--timeline-steps", type=int, default=10,
                     help="steps of the per-stage timeline pass (0: skip)")
     ap.add_argument("--parity-rows", type=int, default=256, help="output rows checked per rank")
-    ap.add_argument("--e2e-chunks", type=int, default=0,
-                    help="pieces per host batch in the e2e leg (0: 4 from 4096 tokens per rank, else 2)")
+    ap.add_argument("--e2e-chunks", type=int, default=1, help="pieces per host batch in the e2e leg")
+    ap.add_argument("--e2e-depth", type=int, default=2,
+                    help="device buffer sets the e2e leg's consecutive steps rotate through")
     ap.add_argument("--force-simt", action="store_true")
-    ap.add_argument("--dispatch-per-warp", action="store_true",
-                    help="dispatch with one warp per token instead of the streaming engine")
+    ap.add_argument("--dispatch-stream", action="store_true",
+                    help="dispatch with the streaming engine instead of one warp per token")
     ap.add_argument("--e2e-graph", choices=["on", "off"], default="off",
                     help="capture the e2e host pipeline as one CUDA graph per step "
                          "(measured slower at N=1 and 2: consecutive steps stop overlapping)")
@@ -346,8 +347,8 @@ def main_b200(a):
                 dtype=torch.bfloat16, device=local, timeout_ms=20000)
     if a.force_simt:
         comm.set_option("force_simt", 1)
-    if a.dispatch_per_warp:
-        comm.set_option("dispatch_per_warp", 1)
+    if a.dispatch_stream:
+        comm.set_option("dispatch_per_warp", 0)
     from miniep_b200 import Placement
     comm.install(Placement.naive(1, E, world))
     # profiling pass: the global per-expert load of these tokens
@@ -491,18 +492,21 @@ def main_b200(a):
     if not a.no_e2e:
         h_host = h.cpu().pin_memory()
         out_host = torch.empty_like(h_host).pin_memory()
-        chunks = a.e2e_chunks or (4 if n >= 4096 else 2)
+        chunks = a.e2e_chunks
         sblk = StreamedMoEBlock(be, n, router_w, rm, bias=bias, chunks=chunks, norm_w=nw,
-                                eps=NORM_EPS)
+                                eps=NORM_EPS, depth=a.e2e_depth)
         graphed = a.e2e_graph == "on"
         if graphed:
             sblk.capture(None, h_host, out_host)  # one graph launch per step
 
         def e2e_step():
-            sblk(None, h_host, out_host)
+            # the next step's copy in and this step's copy out overlap the steps
+            # around them; the timed region ends once the last copy out is done
+            sblk(None, h_host, out_host, wait_output=False)
 
         for _ in range(max(1, a.warmup)):
             e2e_step()
+        torch.cuda.current_stream().wait_event(sblk.done)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -510,6 +514,7 @@ def main_b200(a):
         e0.record()
         for _ in range(a.steps):
             e2e_step()
+        torch.cuda.current_stream().wait_event(sblk.done)
         e1.record()
         torch.cuda.synchronize()
         te = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev, dtype=torch.float64)
@@ -519,10 +524,10 @@ def main_b200(a):
                "h2d_bytes_per_step": h_host.numel() * 2,
                "d2h_bytes_per_step": out_host.numel() * 2,
                "ms_per_step": te.item(),
-               "path": f"StreamedMoEBlock: h from pinned host memory in {chunks} pieces, "
-                       "copies overlapping the pieces' steps"
-                       + (", one CUDA graph per step" if graphed else
-                          ", eager (consecutive steps overlap)")}
+               "path": f"StreamedMoEBlock: h from pinned host memory ({chunks} piece(s), "
+                       f"{a.e2e_depth} device buffer sets), each step's copy in and copy out "
+                       "overlapping the neighbouring steps"
+                       + (", one CUDA graph per step" if graphed else "")}
         comm.check()
         del sblk
     clk = clocks.stop()

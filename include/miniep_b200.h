@@ -56,7 +56,7 @@ const char* mep_last_error(const mep_ctx* ctx);
  * the round-robin state and the routing statistics.
  *   replaces: Comm() + EPStats(L, E) + the per-layer EPMoEBackend state
  *             (miniep/ep.py:110-118, ep.py:164-173, ep.py:193-208,
- *              construction in miniep/worker.py:76-91)
+ *              construction in miniep/worker.py:76-95)
  * max_tokens: largest token count per call on this rank.
  * recv_capacity_rows: receive-buffer rows (0 = worst case, every entry of
  *             every rank landing here plus per-expert padding).

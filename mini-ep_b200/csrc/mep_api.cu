@@ -43,7 +43,7 @@ struct mep_ctx {
   unsigned long long timeout_ns = 10ull * 1000 * 1000 * 1000;
   int force_simt = 0;
   int tc_single_cta = 0;
-  int dispatch_per_warp = 0;  // 1: one warp per token (k_dispatch) instead of the streaming engine
+  int dispatch_per_warp = 1;  // 0: the streaming engine (k_dispatch_stream) instead of one warp per token
   int router_no_tc = 0;       // 1: never the tcgen05 router
   std::vector<int> placed, n_local_l;
   int cur_layer = -1, stage = 0;

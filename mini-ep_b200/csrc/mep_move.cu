@@ -159,6 +159,7 @@ constexpr int kDspWarps = 8;      // warp 0 loads, warps 1..7 place
 constexpr int kDspPending = 4;    // bulk groups a placing warp keeps in flight, at most
 constexpr int kDspMaxSlots = 64;  // ring slots (fewer when the rows are long)
 constexpr unsigned long long kDspWaitNs = 2000000000ull;
+constexpr int kDspChunkTok = 256;  // tokens whose slots are resolved together
 
 __device__ __forceinline__ void bulk_wait_read_pending(int keep) {
   switch (keep) {  // wait_group.read takes an immediate
@@ -178,7 +179,10 @@ __global__ void __launch_bounds__(32 * kDspWarps, 1) k_dispatch_stream(
   extern __shared__ __align__(128) uint8_t dsmem[];
   __shared__ uint64_t full[kDspMaxSlots], empty[kDspMaxSlots];
   __shared__ int pend_slot[kDspWarps][kDspPending];
+  __shared__ int8_t s_dst[kDspChunkTok * kMaxTopk];   // a chunk's resolved slots
+  __shared__ int32_t s_pos[kDspChunkTok * kMaxTopk];
   __shared__ int abort_flag;
+  __shared__ int chunk_go;  // placing warps: go on to the next chunk
   const int lane = lane_id(), wp = warp_id();
   tl_begin(tl, kTlDispatch);
   const int64_t per = (n + gridDim.x - 1) / gridDim.x;
@@ -217,55 +221,77 @@ __global__ void __launch_bounds__(32 * kDspWarps, 1) k_dispatch_stream(
       }
     }
   } else {
+    // placing warps: resolve a chunk's slots together (all of their global
+    // loads in flight at once), then place its tokens round-robin
+    const int ptid = threadIdx.x - 32, nplace = (kDspWarps - 1) * 32;
     int pend = 0, head = 0;  // lane 0: groups issued and not yet known read
-    for (int64_t i = wp - 1; i < cnt; i += kDspWarps - 1) {
-      const int64_t t = t0 + i;
-      const int sl = (int)(i % nslots);
-      const uint32_t ph = (uint32_t)(i / nslots) & 1u;
-      int my_d = -1;
-      int64_t my_pos = 0;
-      if (lane < topk)
-        resolve_slot(t * topk + lane, rank, topk_idx, ent_dest, ent_grp, lay, peers, my_d, my_pos);
-      bool first_remote = my_d >= 0 && my_d != rank;
-      for (int j = 0; j < topk; ++j) {
-        const int dj = __shfl_sync(0xffffffffu, my_d, j);
-        if (j < lane && dj == my_d) first_remote = false;
+    bool ok_all = true;
+    for (int64_t c0 = 0; c0 < cnt && ok_all; c0 += kDspChunkTok) {
+      const int ct = (int)min((int64_t)kDspChunkTok, cnt - c0);
+      for (int i = ptid; i < ct * topk; i += nplace) {
+        int d = -1;
+        int64_t pos = 0;
+        resolve_slot((t0 + c0) * topk + i, rank, topk_idx, ent_dest, ent_grp, lay, peers, d, pos);
+        s_dst[i] = (int8_t)d;
+        s_pos[i] = (int32_t)pos;
       }
-      const unsigned remote = __ballot_sync(0xffffffffu, first_remote);
-      const unsigned local = __ballot_sync(0xffffffffu, my_d == rank);
-      int ok = 1;
-      if (lane == 0) ok = mbar_wait_for(&full[sl], ph, kDspWaitNs, &abort_flag);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        if (lane == 0) set_err(err, kErrPipeline);
-        break;
-      }
-      const uint8_t* row = dsmem + (size_t)sl * row_bytes;
-      for (int s = 0; s < topk; ++s) {
-        const int d = __shfl_sync(0xffffffffu, my_d, s);
-        const int64_t pos = __shfl_sync(0xffffffffu, my_pos, s);
+      asm volatile("bar.sync 1, %0;" ::"n"((kDspWarps - 1) * 32) : "memory");
+      for (int i = wp - 1; i < ct; i += kDspWarps - 1) {
+        const int64_t ti = c0 + i;  // token index within this CTA's range
+        const int64_t t = t0 + ti;
+        const int sl = (int)(ti % nslots);
+        const uint32_t ph = (uint32_t)(ti / nslots) & 1u;
+        const int my_d = lane < topk ? s_dst[i * topk + lane] : -1;
+        const int64_t my_pos = lane < topk ? s_pos[i * topk + lane] : 0;
+        bool first_remote = my_d >= 0 && my_d != rank;
+        for (int j = 0; j < topk; ++j) {
+          const int dj = __shfl_sync(0xffffffffu, my_d, j);
+          if (j < lane && dj == my_d) first_remote = false;
+        }
+        const unsigned remote = __ballot_sync(0xffffffffu, first_remote);
+        const unsigned local = __ballot_sync(0xffffffffu, my_d == rank);
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait_for(&full[sl], ph, kDspWaitNs, &abort_flag);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          if (lane == 0) set_err(err, kErrPipeline);
+          ok_all = false;
+          break;
+        }
+        const uint8_t* row = dsmem + (size_t)sl * row_bytes;
+        for (int s = 0; s < topk; ++s) {
+          const int d = __shfl_sync(0xffffffffu, my_d, s);
+          const int64_t pos = __shfl_sync(0xffffffffu, my_pos, s);
+          if (lane == 0) {
+            if ((local >> s) & 1u)
+              bulk_store_s2g(static_cast<uint8_t*>(peers.recv_x[rank]) + pos * row_bytes, row,
+                             (uint32_t)row_bytes);
+            else if ((remote >> s) & 1u)
+              bulk_store_s2g(static_cast<uint8_t*>(peers.land[d]) +
+                                 ((int64_t)rank * max_tokens + t) * row_bytes,
+                             row, (uint32_t)row_bytes);
+          }
+        }
         if (lane == 0) {
-          if ((local >> s) & 1u)
-            bulk_store_s2g(static_cast<uint8_t*>(peers.recv_x[rank]) + pos * row_bytes, row,
-                           (uint32_t)row_bytes);
-          else if ((remote >> s) & 1u)
-            bulk_store_s2g(static_cast<uint8_t*>(peers.land[d]) +
-                               ((int64_t)rank * max_tokens + t) * row_bytes,
-                           row, (uint32_t)row_bytes);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");  // may be empty
+          pend_slot[wp][(head + pend) % kDspPending] = sl;
+          if (++pend > pending - 1) {
+            // all but the newest pending-1 groups have read shared memory
+            bulk_wait_read_pending(pending - 1);
+            mbar_arrive(&empty[pend_slot[wp][head]]);
+            head = (head + 1) % kDspPending;
+            --pend;
+          }
         }
+        __syncwarp();
       }
-      if (lane == 0) {
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");  // may be empty
-        pend_slot[wp][(head + pend) % kDspPending] = sl;
-        if (++pend > pending - 1) {
-          // all but the newest pending-1 groups have read shared memory
-          bulk_wait_read_pending(pending - 1);
-          mbar_arrive(&empty[pend_slot[wp][head]]);
-          head = (head + 1) % kDspPending;
-          --pend;
-        }
-      }
-      __syncwarp();
+      // every placing warp is done with this chunk's slots (also after an
+      // abort: every placing warp reaches both barriers of a chunk); one
+      // thread reads the abort flag so that all take the same branch
+      asm volatile("bar.sync 1, %0;" ::"n"((kDspWarps - 1) * 32) : "memory");
+      if (ptid == 0) chunk_go = !*(volatile int*)&abort_flag;
+      asm volatile("bar.sync 1, %0;" ::"n"((kDspWarps - 1) * 32) : "memory");
+      ok_all = chunk_go != 0;
     }
     if (lane == 0) {
       asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every copy written
@@ -509,8 +535,9 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
                      int num_sms, int per_warp, int* err, uint64_t* tl, cudaStream_t st) {
   const int row_bytes = hidden * (dtype == kBF16 ? 2 : 4);
   if (!per_warp) {
-    // ring slots within ~200 KB of dynamic shared memory
-    int nslots = (200 * 1024) / row_bytes;
+    // ring slots within ~180 KB of dynamic shared memory (the chunk's
+    // resolved slots take another 20 KB of static shared memory)
+    int nslots = (180 * 1024) / row_bytes;
     if (nslots > kDspMaxSlots) nslots = kDspMaxSlots;
     if (nslots < 2) nslots = 2;
     const size_t smem = (size_t)nslots * row_bytes;

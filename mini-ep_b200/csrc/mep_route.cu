@@ -23,6 +23,7 @@ namespace {
 
 constexpr int kRouteThreads = kRouteChunkTokens;  // one token per thread in the histogram pass
 constexpr int kRouteWarps = kRouteThreads / 32;
+constexpr int kRoutePrefetch = 8;  // independent loads a thread keeps in flight
 
 __device__ __forceinline__ int entry_expert(const int64_t* idx, const uint8_t* valid, int64_t f,
                                             int k, int64_t n, int E, int* err) {
@@ -360,9 +361,14 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   __shared__ int wcnt[kRouteWarps][kMaxExperts];
   __shared__ int wbase[kRouteWarps][kMaxExperts];
   __shared__ int cnt[kMaxWorld * kMaxExperts];
+  __shared__ int s_nrep[kMaxExperts];
+  __shared__ int s_own[kMaxExperts * kMaxWorld];
   __shared__ int any_rep;
   const int wp = warp_id(), lane = lane_id();
   const int b = blockIdx.x;
+  // the last CTA has no tokens: it publishes the counts and lays out the
+  // receive side while the others rank their entries
+  const bool finalizer = b == (int)gridDim.x - 1;
   const int64_t t_beg = min((int64_t)b * tpc, n), t_end = min(t_beg + tpc, n);
   tl_begin(tl, kTlRoute);
 
@@ -372,17 +378,28 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     hist[e] = 0;
     base[e] = 0;
     tot[e] = 0;
-    rr_mod[e] = (int)(((rr[e] % nrep[e]) + nrep[e]) % nrep[e]);  // >= 0 for any rr
+    const int nr = nrep[e];
+    s_nrep[e] = nr;
+    rr_mod[e] = (int)(((rr[e] % nr) + nr) % nr);  // >= 0 for any rr
   }
+  for (int i = threadIdx.x; i < E * kMaxWorld; i += blockDim.x) s_own[i] = owners[i];
   __syncthreads();
   // lanes holding the same expert add once (skewed routing piles entries on
-  // a few experts, so one shared counter would take most of the atomics)
+  // a few experts, so one shared counter would take most of the atomics);
+  // each thread keeps kRoutePrefetch loads in flight
   const unsigned lt_mask = (1u << lane) - 1u;
-  for (int64_t f0 = t_beg * k; f0 < t_end * k; f0 += blockDim.x) {
-    const int64_t f = f0 + threadIdx.x;
-    const int e = f < t_end * k ? entry_expert(idx, valid, f, k, n, E, wc.err) : -1;
-    const unsigned same = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && (same & lt_mask) == 0) atomicAdd(&hist[e], __popc(same));
+  for (int64_t f0 = t_beg * k; f0 < t_end * k; f0 += (int64_t)blockDim.x * kRoutePrefetch) {
+    int ev[kRoutePrefetch];
+#pragma unroll
+    for (int j = 0; j < kRoutePrefetch; ++j) {
+      const int64_t f = f0 + (int64_t)j * blockDim.x + threadIdx.x;
+      ev[j] = f < t_end * k ? entry_expert(idx, valid, f, k, n, E, wc.err) : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < kRoutePrefetch; ++j) {
+      const unsigned same = __match_any_sync(0xffffffffu, ev[j]);
+      if (ev[j] >= 0 && (same & lt_mask) == 0) atomicAdd(&hist[ev[j]], __popc(same));
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_hist[(int64_t)b * E + e] = hist[e];
@@ -399,13 +416,22 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   // ---- phase 2: prefix of the earlier CTAs' counts and the totals
   {
     const int parts = blockDim.x / E > 0 ? blockDim.x / E : 1;
+    const int G = (int)gridDim.x;
     for (int i = threadIdx.x; i < parts * E; i += blockDim.x) {
       const int e = i % E, part = i / E;
       int bsum = 0, tsum = 0;
-      for (int c = part; c < (int)gridDim.x; c += parts) {
-        const int v = __ldcg(chunk_hist + (int64_t)c * E + e);
-        tsum += v;
-        if (c < b) bsum += v;
+      for (int c0 = part; c0 < G; c0 += parts * kRoutePrefetch) {
+        int v[kRoutePrefetch];
+#pragma unroll
+        for (int j = 0; j < kRoutePrefetch; ++j) {
+          const int c = c0 + j * parts;
+          v[j] = c < G ? __ldcg(chunk_hist + (int64_t)c * E + e) : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < kRoutePrefetch; ++j) {
+          tsum += v[j];
+          if (c0 + j * parts < b) bsum += v[j];
+        }
       }
       if (bsum) atomicAdd(&base[e], bsum);
       if (tsum) atomicAdd(&tot[e], tsum);
@@ -413,20 +439,19 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   }
   __syncthreads();
 
-  uint32_t step = 0;  // CTA 0: the sequence number of this layer step
-  if (b == 0) {
+  if (finalizer) {
     // finalize: counts per (dest, expert), rr, stats, publish
-    step = *seq + 1u;
+    const uint32_t step = *seq + 1u;
     for (int i = threadIdx.x; i < world * E; i += blockDim.x) cnt[i] = 0;
     for (int e = threadIdx.x; e < E; e += blockDim.x)
-      if (nrep[e] > 1) any_rep = 1;
+      if (s_nrep[e] > 1) any_rep = 1;
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
       const int c = tot[e];
-      const int nr = nrep[e];
+      const int nr = s_nrep[e];
       const int rr0 = rr_mod[e];
       for (int j = 0; j < nr; ++j) {
-        const int d = owners[e * kMaxWorld + j];
+        const int d = s_own[e * kMaxWorld + j];
         const int w0 = ((j - rr0) % nr + nr) % nr;
         cnt[d * E + e] = c > w0 ? (c - w0 - 1) / nr + 1 : 0;
       }
@@ -448,6 +473,12 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
       *seq = step;
       tl_mark(tl, kTlCountsSent);
     }
+    // the receive layout, once every rank's counts are in
+    extern __shared__ int route_dyn[];  // world * world * E counts for the layout pass
+    layout_block(world, rank, E, owners, nrep, cnt_in, flags, recv_per_layer, cap_rows, lay,
+                 step, wc, route_dyn);
+    __syncthreads();
+    if (threadIdx.x == 0) tl_mark(tl, kTlLayout);
   }
 
   // ---- ranking, 256 tokens per round (8 warps x 32 tokens)
@@ -458,9 +489,17 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     const int64_t t0 = r0 + wp * 32;
     const int64_t f0 = t0 * k;
     const int64_t f_end = min(r0 + kRouteChunkTokens, t_end) * k;
-    for (int r = 0; r < k; ++r) {
+    // this warp's entries of the round, loaded once for both passes
+    int ev[kMaxTopk];
+#pragma unroll
+    for (int r = 0; r < kMaxTopk; ++r) {
       const int64_t f = f0 + r * 32 + lane;
-      const int e = f < f_end ? entry_expert(idx, valid, f, k, n, E, nullptr) : -1;
+      ev[r] = (r < k && f < f_end) ? entry_expert(idx, valid, f, k, n, E, nullptr) : -1;
+    }
+#pragma unroll
+    for (int r = 0; r < kMaxTopk; ++r) {
+      if (r >= k) break;
+      const int e = ev[r];
       const unsigned same = __match_any_sync(0xffffffffu, e);
       if (e >= 0 && (same & lt_mask) == 0) wcnt[wp][e] += __popc(same);
     }
@@ -475,17 +514,19 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
       hist[e] = run;  // this round's total, added to base after the pass
     }
     __syncthreads();
-    for (int r = 0; r < k; ++r) {
+#pragma unroll
+    for (int r = 0; r < kMaxTopk; ++r) {
+      if (r >= k) break;
       const int64_t f = f0 + r * 32 + lane;
-      const int e = f < f_end ? entry_expert(idx, valid, f, k, n, E, nullptr) : -1;
+      const int e = ev[r];
       const unsigned peers_mask = __match_any_sync(0xffffffffu, e);
       const int rank_in_round = __popc(peers_mask & lt_mask);
       int dest = -1, grp = 0;
       if (e >= 0) {
         const int within = base[e] + wbase[wp][e] + wcnt[wp][e] + rank_in_round;
-        const int nr = nrep[e];
+        const int nr = s_nrep[e];
         const int slot = (rr_mod[e] + within) % nr;
-        dest = owners[e * kMaxWorld + slot];
+        dest = s_own[e * kMaxWorld + slot];
         grp = within / nr;
       }
       __syncwarp();
@@ -499,15 +540,6 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] += hist[e];
     __syncthreads();
-  }
-  if (b == 0) {
-    // the receive layout, once every rank's counts are in: after this CTA's
-    // own ranking, which overlaps the peers' publishing
-    extern __shared__ int route_dyn[];  // world * world * E counts for the layout pass
-    layout_block(world, rank, E, owners, nrep, cnt_in, flags, recv_per_layer, cap_rows, lay,
-                 step, wc, route_dyn);
-    __syncthreads();
-    if (threadIdx.x == 0) tl_mark(tl, kTlLayout);
   }
   tl_end(tl, kTlRoute + 1);
 }
@@ -527,11 +559,13 @@ void launch_route(int64_t n, int topk, int experts, int world, int rank,
                   const int32_t* cnt_in_local, const uint32_t* flags_local,
                   int64_t* recv_per_layer_l, int64_t cap_rows, Layout* layout, WaitCfg wc,
                   uint64_t* tl, cudaStream_t st) {
-  // one CTA per 256-token round, at most one per SM (all resident for the grid barrier)
+  // one CTA per 256-token round, at most one per SM (all resident for the
+  // grid barrier), plus the finalizing CTA
   const int64_t rounds = (n + kRouteChunkTokens - 1) / kRouteChunkTokens;
-  int64_t grid = rounds < num_sms ? rounds : num_sms;
-  if (grid < 1) grid = 1;
-  const int64_t tpc = (rounds + grid - 1) / grid * kRouteChunkTokens;
+  int64_t chunks = rounds < num_sms - 1 ? rounds : num_sms - 1;
+  if (chunks < 1) chunks = 1;
+  const int64_t grid = chunks + 1;
+  const int64_t tpc = (rounds + chunks - 1) / chunks * kRouteChunkTokens;
   const size_t dyn = (size_t)world * world * experts * sizeof(int);  // <= 32 KiB
   static size_t dyn_set = 0;
   if (dyn > dyn_set) {

@@ -510,38 +510,57 @@ class GraphedMoEBlock:
 class StreamedMoEBlock:
     """``GraphedMoEBlock`` for token batches that live in (pinned) host memory.
 
-    The batch is cut into ``chunks`` pieces, each with its own captured layer
-    step. Piece i's host-to-device copy runs on one stream, its layer step on
-    the caller's stream and its device-to-host copy on a third, so the copies
-    of one piece overlap the steps of the others (and, across calls, the next
-    batch's first copies overlap this batch's last step). Each piece is one
-    layer call of the reference's contract: routing, replica round-robin and
-    stats advance per piece exactly as for consecutive eager calls, and every
-    output row is bit-identical to the unchunked step's.
+    Each call copies the batch from the host, runs the captured layer step and
+    copies the result back. The host-to-device copies run on one stream, the
+    steps on the caller's stream and the device-to-host copies on a third, so
+    the two copy directions (which PCIe carries at the same time) overlap each
+    other and the steps:
 
-    Every rank must use the same ``chunks`` and call in lockstep.
-    ``capture`` records the whole pipeline for fixed pinned buffers into one
-    CUDA graph (consecutive calls then no longer overlap each other, only the
-    pieces of one call do).
+    * ``depth`` sets of device buffers (each with its own captured step) are
+      used round-robin by consecutive calls, so call j+1's input copy and call
+      j-1's output copy run while call j's step computes (default 2);
+    * ``chunks`` cuts each batch into pieces with their own captured steps, so
+      that the pieces of one call overlap each other too (each piece is one
+      layer call of the reference's contract: routing, replica round-robin and
+      stats advance per piece exactly as for consecutive eager calls, and
+      every output row is bit-identical to the unchunked step's).
+
+    ``__call__(..., wait_output=True)`` makes the caller's stream wait for
+    this call's output copy (``out_host`` is complete once the stream reaches
+    that point). With ``wait_output=False`` it does not: the next call's step
+    can then overlap this call's output copy, and the caller must wait on
+    ``self.done`` (the last call's output copy) before reading ``out_host`` or
+    changing ``h_host`` / ``x_host``. Every rank must use the same ``chunks``
+    and ``depth`` and call in lockstep. ``capture`` records one call's whole
+    pipeline for fixed pinned buffers into one CUDA graph (consecutive calls
+    then no longer overlap each other, only the pieces of one call do).
     """
 
+    class _Set:
+        def __init__(self, blocks):
+            self.blocks = blocks
+            ev = lambda: [torch.cuda.Event() for _ in blocks]  # noqa: E731
+            self.loaded, self.stepped, self.inputs_free, self.output_free = ev(), ev(), ev(), ev()
+
     def __init__(self, backend: "EPMoEBackend", n_tokens: int, router_w,
-                 residual_multiplier: float, bias=None, chunks: int = 4, norm_w=None,
-                 eps: float = 1e-6):
-        if n_tokens < 1 or chunks < 1:
-            raise ValueError("StreamedMoEBlock: n_tokens and chunks must be positive")
+                 residual_multiplier: float, bias=None, chunks: int = 1, norm_w=None,
+                 eps: float = 1e-6, depth: int = 2):
+        if n_tokens < 1 or chunks < 1 or depth < 1:
+            raise ValueError("StreamedMoEBlock: n_tokens, chunks and depth must be positive")
         chunks = min(chunks, n_tokens)
         base, extra = divmod(n_tokens, chunks)
         self.sizes = [base + (1 if i < extra else 0) for i in range(chunks)]
         self.n = n_tokens
         self.from_h = norm_w is not None
-        self.blocks = [GraphedMoEBlock(backend, m, router_w, residual_multiplier, bias=bias,
-                                       norm_w=norm_w, eps=eps)
-                       for m in self.sizes]
+        self.sets = [self._Set([GraphedMoEBlock(backend, m, router_w, residual_multiplier,
+                                                bias=bias, norm_w=norm_w, eps=eps)
+                                for m in self.sizes])
+                     for _ in range(depth)]
+        self.blocks = self.sets[0].blocks
         self.copy_in = torch.cuda.Stream()
         self.copy_out = torch.cuda.Stream()
-        ev = lambda: [torch.cuda.Event() for _ in self.sizes]  # noqa: E731
-        self.loaded, self.stepped, self.inputs_free, self.output_free = ev(), ev(), ev(), ev()
+        self.done = torch.cuda.Event()
+        self.calls = 0
 
     def _check(self, x_host, h_host, out_host):
         if (x_host is None) != self.from_h:
@@ -550,38 +569,43 @@ class StreamedMoEBlock:
                 out_host.shape[0] != self.n:
             raise ValueError(f"StreamedMoEBlock: expected {self.n} tokens")
 
-    def _enqueue(self, x_host, h_host, out_host, capturing: bool):
+    def _enqueue(self, st, x_host, h_host, out_host, capturing: bool, wait_output: bool):
         cur = torch.cuda.current_stream()
         if capturing:  # the side streams join the capture
             self.copy_in.wait_stream(cur)
             self.copy_out.wait_stream(cur)
         off = 0
-        for i, (blk, m) in enumerate(zip(self.blocks, self.sizes)):
+        for i, (blk, m) in enumerate(zip(st.blocks, self.sizes)):
             rows = slice(off, off + m)
             off += m
             with torch.cuda.stream(self.copy_in):
                 if not capturing:
-                    self.copy_in.wait_event(self.inputs_free[i])  # last call's step i read blk.x / blk.h
+                    self.copy_in.wait_event(st.inputs_free[i])  # this set's last step read blk.x / blk.h
                 if x_host is not None:
                     blk.x.copy_(x_host[rows], non_blocking=True)
                 blk.h.copy_(h_host[rows], non_blocking=True)
-                self.loaded[i].record(self.copy_in)
-            cur.wait_event(self.loaded[i])
+                st.loaded[i].record(self.copy_in)
+            cur.wait_event(st.loaded[i])
             if capturing:
                 blk._step()
             else:
-                cur.wait_event(self.output_free[i])  # last call's copy-out of blk.h_out is done
+                cur.wait_event(st.output_free[i])  # this set's last copy-out of blk.h_out is done
+                _check_replay(blk.backend, blk.captured)
                 blk.graph.replay()
-                self.inputs_free[i].record(cur)
-            self.stepped[i].record(cur)
+                st.inputs_free[i].record(cur)
+            st.stepped[i].record(cur)
             with torch.cuda.stream(self.copy_out):
-                self.copy_out.wait_event(self.stepped[i])
+                self.copy_out.wait_event(st.stepped[i])
                 out_host[rows].copy_(blk.h_out, non_blocking=True)
                 if not capturing:
-                    self.output_free[i].record(self.copy_out)
+                    st.output_free[i].record(self.copy_out)
         if capturing:
             cur.wait_stream(self.copy_in)
-        cur.wait_stream(self.copy_out)
+            cur.wait_stream(self.copy_out)
+            return
+        self.done.record(self.copy_out)
+        if wait_output:
+            cur.wait_stream(self.copy_out)
 
     def capture(self, x_host, h_host, out_host):
         """Record the whole per-call pipeline (copies in, the pieces' layer
@@ -594,24 +618,27 @@ class StreamedMoEBlock:
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            self._enqueue(x_host, h_host, out_host, capturing=True)
+            self._enqueue(self.sets[0], x_host, h_host, out_host, capturing=True,
+                          wait_output=True)
         self.graph = g
         self.bound = (None if x_host is None else x_host.data_ptr(), h_host.data_ptr(),
                       out_host.data_ptr())
 
-    def __call__(self, x_host, h_host, out_host):
-        """Enqueue ``out_host = h_host + moe(x_host) * rm`` on the current
-        stream. The host tensors must be pinned for the copies to overlap;
-        ``out_host`` is complete once the current stream reaches this point."""
+    def __call__(self, x_host, h_host, out_host, wait_output: bool = True):
+        """Enqueue ``out_host = h_host + moe(x_host) * rm`` (see the class
+        notes for ``wait_output``). The host tensors must be pinned for the
+        copies to overlap."""
         self._check(x_host, h_host, out_host)
-        for blk in self.blocks:
-            _check_replay(blk.backend, blk.captured)
         if getattr(self, "graph", None) is not None and self.bound == (
                 None if x_host is None else x_host.data_ptr(), h_host.data_ptr(),
                 out_host.data_ptr()):
+            for blk in self.sets[0].blocks:
+                _check_replay(blk.backend, blk.captured)
             self.graph.replay()
             return out_host
-        self._enqueue(x_host, h_host, out_host, capturing=False)
+        st = self.sets[self.calls % len(self.sets)]
+        self.calls += 1
+        self._enqueue(st, x_host, h_host, out_host, capturing=False, wait_output=wait_output)
         return out_host
 
 

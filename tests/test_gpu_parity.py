@@ -28,6 +28,17 @@ BF16_ATOL = 2e-2       # bf16 outputs vs an fp32 reference, max-abs, for outputs
 ROUTER_ROUNDING_ROWS = 0.005
 
 
+def logit_step(logits, bias=None):
+    """One bf16 rounding step of a router logit, from either of its two
+    roundings: the dot product (magnitude |logit - bias|) rounds to bf16, then
+    the bias is added and the sum rounds again. Two fp32 sums of the same dot
+    product that round to neighbouring bf16 values give logits at most one
+    step of each apart (with cancellation against the bias the first step can
+    exceed the logit's own)."""
+    b = 0.0 if bias is None else bias.to(torch.bfloat16).float()
+    return ((logits - b).abs() + logits.abs()).clamp_min(2.0 ** -20) * 2.0 ** -7
+
+
 def bf16_tol(ref32):
     """2e-2 max-abs, scaled by the output magnitude when it exceeds 1: shape
     (b) outputs reach |3.6| and the reference's own bf16 path is already
@@ -81,8 +92,7 @@ def test_router_bf16_skewed(shape, n):
     idx, gate, logits = idx.cpu(), gate.cpu(), logits.cpu()
     ref_idx, ref_gate, ref_logits = O.router_topk(lb.x, lb.router, sh["topk"], bias)
     # logits: fp32 accumulation in another order, then the same rounding
-    ulp = ref_logits.float().abs().clamp_min(2.0 ** -20) * 2.0 ** -7
-    assert torch.all((logits - ref_logits.float()).abs() <= ulp)
+    assert torch.all((logits - ref_logits.float()).abs() <= logit_step(ref_logits.float(), bias))
     same_row = (logits == ref_logits.float()).all(dim=1)
     if n >= 64:
         assert same_row.float().mean() > 0.9
@@ -127,8 +137,7 @@ def test_router_tcgen05_and_warp_kernels_agree(shape):
         got[no_tc] = [t.cpu() for t in router_topk(comm, x, w, bias, return_logits=True)]
     comm.check()
     (i_tc, g_tc, l_tc), (i_w, g_w, l_w) = got[0], got[1]
-    ulp = l_w.abs().clamp_min(2.0 ** -20) * 2.0 ** -7
-    assert torch.all((l_tc - l_w).abs() <= ulp)
+    assert torch.all((l_tc - l_w).abs() <= logit_step(l_w, bias.cpu()))
     same = (l_tc == l_w).all(dim=1)
     assert same.float().mean() > 0.9
     assert torch.equal(i_tc[same], i_w[same])
@@ -167,8 +176,7 @@ def test_router_bf16_rows_not_16_byte_aligned():
     idx, gate, logits = router_topk(comm, x, lb.router.cuda(), return_logits=True)
     idx, logits = idx.cpu(), logits.cpu()
     _, _, ref_logits = O.router_topk(lb.x, lb.router, sh["topk"])
-    ulp = ref_logits.float().abs().clamp_min(2.0 ** -20) * 2.0 ** -7
-    assert torch.all((logits - ref_logits.float()).abs() <= ulp)
+    assert torch.all((logits - ref_logits.float()).abs() <= logit_step(ref_logits.float()))
     assert torch.equal(idx, O.topk_lowest_index(logits, sh["topk"]))
 
 
@@ -520,4 +528,17 @@ def test_moe_block_from_h_is_norm_then_block():
     sblk(None, h_host, out_host)
     torch.cuda.synchronize()
     assert torch.equal(out_host, out.cpu())
+    # two buffer sets, calls that do not wait for their output copies: each
+    # call's rows once `done` has passed, over consecutive calls
+    h2 = synth.make_tokens(n, H, seed=26, dtype=torch.bfloat16).cuda()
+    want2, *_ = be.moe_block_from_h(h2, w, 1e-6, router, rm, bias=bias)
+    pblk = StreamedMoEBlock(be, n, router, rm, bias=bias, chunks=1, norm_w=w, eps=1e-6, depth=2)
+    ins = [h.cpu().pin_memory(), h2.cpu().pin_memory(), h.cpu().pin_memory()]
+    outs = [torch.empty_like(ins[0]).pin_memory() for _ in ins]
+    for hi, oi in zip(ins, outs):
+        pblk(None, hi, oi, wait_output=False)
+    torch.cuda.current_stream().wait_event(pblk.done)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], out.cpu()) and torch.equal(outs[2], out.cpu())
+    assert torch.equal(outs[1], want2.cpu())
     be.comm.check()
