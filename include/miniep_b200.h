@@ -233,6 +233,8 @@ int mep_set_option(mep_ctx* ctx, const char* name, int64_t value);
 #define MEP_TL_GEMM2 16       /* expert GEMM2 + return stores start, end */
 #define MEP_TL_RESULTS_IN 18  /* every owner's results for this rank landed */
 #define MEP_TL_COMBINE 19     /* combine start, end */
+#define MEP_TL_ROUTE_HIST 21  /* routing: the last CTA's histogram written */
+#define MEP_TL_ROUTE_SYNC 22  /* routing: the finalizing CTA left the grid barrier */
 #define MEP_TL_SLOTS 24
 int mep_read_timeline(mep_ctx* ctx, uint64_t* out, void* stream);
 

@@ -188,23 +188,33 @@ constexpr unsigned long long kWaitNs = 2000000000ull;  // bounded mbarrier waits
 // Per-variant geometry. Single CTA: a 128x256 tile per CTA, the CTA loads
 // 128 A rows + 256 B rows per k-block. CTA pair: a 256x256 tile per 2-CTA
 // cluster, each CTA loads its 128 A rows + 128 of the B rows.
-template <bool PAIR>
+// A-stationary (AST, CTA pairs, K <= 512): a pair works through all N blocks
+// of one 256-row tile in a row; its A rows stay in shared memory (one slot
+// per k-block) across them, and only B streams through the stage ring. The
+// operands loaded per row tile drop from N blocks x (A + B) to A + N blocks
+// x B (GEMM2 of shape (a): 640 KiB instead of 1 MiB per CTA), and the stage
+// loads, not the tensor pipe, are what bound this kernel otherwise.
+constexpr int AST_SLOTS = 8;  // resident A k-blocks: K <= 512
+template <bool PAIR, bool AST = false>
 struct Geo {
   static constexpr int TILE_M = PAIR ? 256 : 128;
   static constexpr int B_ROWS = PAIR ? 128 : 256;         // B rows held by one CTA
-  static constexpr int STAGE = A_TILE + B_ROWS * BK * 2;  // bytes per stage per CTA
-  static constexpr int STAGES = PAIR ? 6 : 4;
-  static constexpr int DATA = STAGES * STAGE;
+  static constexpr int A_REGION = AST ? AST_SLOTS * A_TILE : 0;
+  static constexpr int STAGE = (AST ? 0 : A_TILE) + B_ROWS * BK * 2;  // bytes per stage per CTA
+  static constexpr int STAGES = AST ? 4 : (PAIR ? 6 : 4);
+  static constexpr int DATA = A_REGION + STAGES * STAGE;
   static constexpr uint32_t TX = (PAIR ? 2 : 1) * STAGE;  // bytes landing on the leader's barrier
+  static constexpr uint32_t TX_A = (PAIR ? 2 : 1) * A_TILE;
   // kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, N=256, M=TILE_M
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
                                     ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(TILE_M >> 4) << 24);
   static constexpr uint32_t TEMPTY_ARRIVALS = EPI_WARPS * (PAIR ? 2 : 1);
 };
 
-template <bool PAIR>
+template <bool PAIR, bool AST = false>
 struct Smem {
-  uint64_t full[Geo<PAIR>::STAGES], empty[Geo<PAIR>::STAGES], tfull[2], tempty[2];
+  uint64_t full[Geo<PAIR, AST>::STAGES], empty[Geo<PAIR, AST>::STAGES], tfull[2], tempty[2];
+  uint64_t a_full[AST_SLOTS], a_empty[AST_SLOTS];  // A-stationary: resident A slots
   uint32_t tmem_base;
   int abort;
   int n_local, total;
@@ -212,21 +222,22 @@ struct Smem {
 };
 // epilogue staging: 32 rows x 128 B per warp, 16-byte chunks XOR-swizzled by row
 constexpr int STAGE_WARP_BYTES = 32 * 128;
-template <bool PAIR>
+template <bool PAIR, bool AST = false>
 __host__ __device__ constexpr int off_stage() {  // 1024-aligned: TMA 128B-swizzle tile source
-  return Geo<PAIR>::DATA + (((int)sizeof(Smem<PAIR>) + 1023) / 1024) * 1024;
+  return Geo<PAIR, AST>::DATA + (((int)sizeof(Smem<PAIR, AST>) + 1023) / 1024) * 1024;
 }
-template <bool PAIR>
+template <bool PAIR, bool AST = false>
 __host__ __device__ constexpr int smem_bytes() {
-  return off_stage<PAIR>() + EPI_WARPS * STAGE_WARP_BYTES + 1024;
+  return off_stage<PAIR, AST>() + EPI_WARPS * STAGE_WARP_BYTES + 1024;
 }
 static_assert(smem_bytes<false>() <= 232448, "single-CTA kernel exceeds shared memory");
 static_assert(smem_bytes<true>() <= 232448, "CTA-pair kernel exceeds shared memory");
+static_assert(smem_bytes<true, true>() <= 232448, "A-stationary kernel exceeds shared memory");
 
 // Bounded wait: false (and the CTA abort flag + device error set) on timeout
 // or when another role of this CTA already gave up.
-template <bool PAIR>
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, Smem<PAIR>* S, int* err) {
+template <class SM>
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, SM* S, int* err) {
   if (mbar_try(b, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 0;; ++it) {
@@ -301,16 +312,26 @@ struct TcArgs {
 
 // MODE 0: GEMM1 + SwiGLU -> act. MODE 1: GEMM2 -> source landing rows.
 // PAIR: one 256-row tile per 2-CTA cluster with tcgen05.mma.cta_group::2.
-template <int MODE, bool PAIR>
+// The i-th tile a unit (CTA or CTA pair) works on: units take tiles
+// round-robin, or, A-stationary, whole row tiles (all their N blocks in order).
+template <bool AST>
+__device__ __forceinline__ int unit_tile(int i, int unit, int nunits, int ntiles_n) {
+  if (!AST) return unit + i * nunits;
+  return (unit + (i / ntiles_n) * nunits) * ntiles_n + i % ntiles_n;
+}
+
+template <int MODE, bool PAIR, bool AST = false>
 __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ CUtensorMap tmA,
                                                        const __grid_constant__ CUtensorMap tmB,
                                                        const __grid_constant__ RetMaps rmaps,
                                                        const TcArgs args) {
-  using G = Geo<PAIR>;
+  using G = Geo<PAIR, AST>;
+  using SM = Smem<PAIR, AST>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  Smem<PAIR>* S = reinterpret_cast<Smem<PAIR>*>(smem + G::DATA);
+  SM* S = reinterpret_cast<SM*>(smem + G::DATA);
+  uint8_t* ring = smem + G::A_REGION;  // the stage ring (after the resident A slots)
   const int wp = warp_id(), lane = lane_id();
   const uint32_t cta = PAIR ? cluster_rank() : 0u;
   const bool leader = cta == 0;
@@ -324,6 +345,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
     for (int b = 0; b < 2; ++b) {
       mbar_init(&S->tfull[b], 1);
       mbar_init(&S->tempty[b], G::TEMPTY_ARRIVALS);  // used in the leader
+    }
+    for (int a = 0; a < AST_SLOTS; ++a) {
+      mbar_init(&S->a_full[a], 1);
+      mbar_init(&S->a_empty[a], 1);
     }
     S->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -376,24 +401,40 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      for (int t = unit; t < total; t += nunits) {
+      for (int i = 0;; ++i) {
+        const int t = unit_tile<AST>(i, unit, nunits, args.ntiles_n);
+        if (t >= total) break;
         const TileCoord c = decode_tile(t, args.ntiles_n, 1, G::TILE_M, G::TILE_M, S->n_local,
                                         S->prefix, S->base, S->rows);
         const int arow = c.row0 + (int)cta * 128;
         const int brow = c.j * args.b_rows_per_expert + c.nb * args.b_step;
+        const uint32_t a_ph = (uint32_t)(i / args.ntiles_n) & 1u;  // AST: row tiles so far
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
+          if (AST && c.nb == 0) {
+            // A slot kb: free once the previous row tile's last N block used it
+            if (!mbar_wait(&S->a_empty[kb], a_ph ^ 1u, S, args.err)) {
+              ok = false;
+              break;
+            }
+            if (leader) mbar_expect_tx(&S->a_full[kb], G::TX_A);
+            const uint32_t abar = map_to_cta(&S->a_full[kb], 0);
+            tma_load_2d<PAIR>(smem + kb * A_TILE, &tmA, kb * BK, arow, abar);
+          }
           if (!mbar_wait(&S->empty[s], ph ^ 1u, S, args.err)) {
             ok = false;
             break;
           }
           if (leader) mbar_expect_tx(&S->full[s], G::TX);
           const uint32_t bar = PAIR ? map_to_cta(&S->full[s], 0) : smem_u32(&S->full[s]);
-          uint8_t* st = smem + s * G::STAGE;
-          tma_load_2d<PAIR>(st, &tmA, kb * BK, arow, bar);
-          if (PAIR) {
+          uint8_t* st = ring + s * G::STAGE;
+          if (AST) {
+            tma_load_2d<PAIR>(st, &tmB, kb * BK, brow + (cta ? args.b_second : 0), bar);
+          } else if (PAIR) {
+            tma_load_2d<PAIR>(st, &tmA, kb * BK, arow, bar);
             tma_load_2d<PAIR>(st + A_TILE, &tmB, kb * BK, brow + (cta ? args.b_second : 0), bar);
           } else {
+            tma_load_2d<PAIR>(st, &tmA, kb * BK, arow, bar);
             tma_load_2d<PAIR>(st + A_TILE, &tmB, kb * BK, brow, bar);
             tma_load_2d<PAIR>(st + A_TILE + A_TILE, &tmB, kb * BK, brow + args.b_second, bar);
           }
@@ -410,8 +451,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
     if (leader && lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      int it = 0;
-      for (int t = unit; t < total; t += nunits, ++it) {
+      for (int it = 0;; ++it) {
+        const int t = unit_tile<AST>(it, unit, nunits, args.ntiles_n);
+        if (t >= total) break;
+        const int nb = t % args.ntiles_n;
+        const uint32_t a_ph = (uint32_t)(it / args.ntiles_n) & 1u;
         const int b = it & 1;
         const uint32_t aph = (uint32_t)(it >> 1) & 1u;
         if (!mbar_wait(&S->tempty[b], aph ^ 1u, S, args.err)) break;
@@ -419,18 +463,26 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
         const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
+          if (AST && nb == 0) {
+            if (!mbar_wait(&S->a_full[kb], a_ph, S, args.err)) {
+              ok = false;
+              break;
+            }
+          }
           if (!mbar_wait(&S->full[s], ph, S, args.err)) {
             ok = false;
             break;
           }
           fence_after();
-          const uint32_t a0 = smem_u32(smem + s * G::STAGE);
-          const uint32_t b0 = a0 + A_TILE;
+          const uint32_t a0 = AST ? smem_u32(smem + kb * A_TILE) : smem_u32(ring + s * G::STAGE);
+          const uint32_t b0 = AST ? smem_u32(ring + s * G::STAGE) : a0 + A_TILE;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             mma_f16<PAIR>(d_tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), G::IDESC,
                           (kb | kk) != 0);
           mma_commit<PAIR>(&S->empty[s]);
+          // the row tile's last N block frees A slot kb for the next row tile
+          if (AST && nb == args.ntiles_n - 1) mma_commit<PAIR>(&S->a_empty[kb]);
           if (++s == G::STAGES) {
             s = 0;
             ph ^= 1u;
@@ -449,9 +501,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
     const int m = q * 32 + lane;
     const uint32_t tempty_leader[2] = {PAIR ? map_to_cta(&S->tempty[0], 0) : smem_u32(&S->tempty[0]),
                                        PAIR ? map_to_cta(&S->tempty[1], 0) : smem_u32(&S->tempty[1])};
-    uint8_t* stage = smem + off_stage<PAIR>() + e * STAGE_WARP_BYTES;
-    int it = 0;
-    for (int t = unit; t < total; t += nunits, ++it) {
+    uint8_t* stage = smem + off_stage<PAIR, AST>() + e * STAGE_WARP_BYTES;
+    for (int it = 0;; ++it) {
+      const int t = unit_tile<AST>(it, unit, nunits, args.ntiles_n);
+      if (t >= total) break;
       const int b = it & 1;
       const uint32_t aph = (uint32_t)(it >> 1) & 1u;
       const TileCoord c = decode_tile(t, args.ntiles_n, 1, G::TILE_M, G::TILE_M, S->n_local,
@@ -634,7 +687,10 @@ int tc_init() {
       cudaFuncSetAttribute(ffn::k_ffn_tc<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            ffn::smem_bytes<true>()) != cudaSuccess ||
       cudaFuncSetAttribute(ffn::k_ffn_tc<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           ffn::smem_bytes<true>()) != cudaSuccess)
+                           ffn::smem_bytes<true>()) != cudaSuccess ||
+      cudaFuncSetAttribute(ffn::k_ffn_tc<1, true, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           ffn::smem_bytes<true, true>()) != cudaSuccess)
     return -2;
   ffn::g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   return 0;
@@ -672,11 +728,11 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
       if ((rc = ffn::make_tmap(&rmaps.m[r], a.peers.ret[r], H, (uint64_t)a.ret_rows, 32)))
         return rc;
     auto launch = [&](auto kernel, bool as_pair, const CUtensorMap& ta, const CUtensorMap& tb,
-                      const ffn::TcArgs& g) -> cudaError_t {
+                      const ffn::TcArgs& g, int smem) -> cudaError_t {
       cudaLaunchConfig_t cfg{};
       cfg.gridDim = dim3((unsigned)(as_pair ? (a.num_sms & ~1) : a.num_sms));
       cfg.blockDim = dim3(ffn::THREADS);
-      cfg.dynamicSmemBytes = as_pair ? ffn::smem_bytes<true>() : ffn::smem_bytes<false>();
+      cfg.dynamicSmemBytes = smem;
       cfg.stream = st;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -687,8 +743,10 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
       cfg.numAttrs = as_pair ? 1 : 0;
       return cudaLaunchKernelEx(&cfg, kernel, ta, tb, rmaps, g);
     };
-    cudaError_t e = pair ? launch(ffn::k_ffn_tc<0, true>, true, tmA1, tmB1, g1)
-                         : launch(ffn::k_ffn_tc<0, false>, false, tmA1, tmB1, g1);
+    cudaError_t e = pair ? launch(ffn::k_ffn_tc<0, true>, true, tmA1, tmB1, g1,
+                                  ffn::smem_bytes<true>())
+                         : launch(ffn::k_ffn_tc<0, false>, false, tmA1, tmB1, g1,
+                                  ffn::smem_bytes<false>());
     if (e != cudaSuccess) return (int)e;
     ffn::TcArgs g2{};
     g2.lay = a.layout;
@@ -705,8 +763,14 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g2.seq = a.seq;
     g2.err = a.err;
     g2.tl = a.tl;
-    e = pair ? launch(ffn::k_ffn_tc<1, true>, true, tmA2, tmB2, g2)
-             : launch(ffn::k_ffn_tc<1, false>, false, tmA2, tmB2, g2);
+    // A-stationary GEMM2 when a row tile's A (K = I columns) fits the resident slots
+    const bool ast = pair && !a.no_ast && I / ffn::BK <= ffn::AST_SLOTS;
+    if (ast)
+      e = launch(ffn::k_ffn_tc<1, true, true>, true, tmA2, tmB2, g2,
+                 ffn::smem_bytes<true, true>());
+    else
+      e = pair ? launch(ffn::k_ffn_tc<1, true>, true, tmA2, tmB2, g2, ffn::smem_bytes<true>())
+               : launch(ffn::k_ffn_tc<1, false>, false, tmA2, tmB2, g2, ffn::smem_bytes<false>());
     if (e != cudaSuccess) return (int)e;
     return (int)cudaGetLastError();
   }

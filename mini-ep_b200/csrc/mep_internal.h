@@ -34,6 +34,8 @@ enum TlSlot : int {
   kTlGemm2 = MEP_TL_GEMM2,
   kTlResultsIn = MEP_TL_RESULTS_IN,
   kTlCombine = MEP_TL_COMBINE,
+  kTlRouteHist = MEP_TL_ROUTE_HIST,
+  kTlRouteSync = MEP_TL_ROUTE_SYNC,
   kTlSlots = MEP_TL_SLOTS,
 };
 
@@ -172,6 +174,7 @@ struct FfnArgs {
   int num_sms;
   int force_simt;           // 1: run the CUDA-core kernels even for bf16
   int tc_single_cta;        // 1: one CTA per 128x256 tile instead of CTA pairs per 256x256
+  int no_ast;               // 1: GEMM2 reloads A per N block (no A-stationary variant)
   int n_local_weights;      // leading extent of w_in / w_out
   int* err;                 // host-mapped device error word
   uint64_t* tl;             // step timeline or null

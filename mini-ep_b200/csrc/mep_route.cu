@@ -403,6 +403,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_hist[(int64_t)b * E + e] = hist[e];
+  tl_end(tl, kTlRouteHist);
   if (!grid_barrier(gs, gridDim.x, wc)) {
     // the barrier timed out (error word set): another CTA's histogram may be
     // missing, so this CTA routes nothing and leaves the round-robin state,
@@ -440,6 +441,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   __syncthreads();
 
   if (finalizer) {
+    if (threadIdx.x == 0) tl_mark(tl, kTlRouteSync);
     // finalize: counts per (dest, expert), rr, stats, publish
     const uint32_t step = *seq + 1u;
     for (int i = threadIdx.x; i < world * E; i += blockDim.x) cnt[i] = 0;

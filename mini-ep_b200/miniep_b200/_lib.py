@@ -20,7 +20,8 @@ IPC_HANDLE_BYTES = 64
 TL_SLOTS = 24
 TL_STAGES = {"norm": 1, "router": 3, "route": 5, "dispatch": 9, "fanout": 12, "gemm1": 14,
              "gemm2": 16, "combine": 19}
-TL_MARKS = {"barrier_end": 0, "counts_sent": 7, "layout": 8, "data_in": 11, "results_in": 18}
+TL_MARKS = {"barrier_end": 0, "counts_sent": 7, "layout": 8, "data_in": 11, "results_in": 18,
+            "route_hist": 21, "route_sync": 22}
 
 _P = C.c_void_p
 _I64 = C.c_int64
