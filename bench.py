@@ -81,8 +81,10 @@ def parse():
     ap.add_argument("--e2e-depth", type=int, default=2,
                     help="device buffer sets the e2e leg's consecutive steps rotate through")
     ap.add_argument("--force-simt", action="store_true")
-    ap.add_argument("--ffn-no-ast", action="store_true",
-                    help="GEMM2 reloads its activation tile per N block (no A-stationary variant)")
+    ap.add_argument("--ffn-ast", action="store_true",
+                    help="A-stationary GEMM2 (keeps a row tile's activations resident)")
+    ap.add_argument("--ffn-prefetch", action="store_true",
+                    help="GEMMs prefetch their next tile's rows into L2")
     ap.add_argument("--dispatch-stream", action="store_true",
                     help="dispatch with the streaming engine instead of one warp per token")
     ap.add_argument("--e2e-graph", choices=["on", "off"], default="off",
@@ -351,8 +353,10 @@ def main_b200(a):
         comm.set_option("force_simt", 1)
     if a.dispatch_stream:
         comm.set_option("dispatch_per_warp", 0)
-    if a.ffn_no_ast:
-        comm.set_option("ffn_no_ast", 1)
+    if a.ffn_ast:
+        comm.set_option("ffn_ast", 1)
+    if a.ffn_prefetch:
+        comm.set_option("ffn_prefetch", 1)
     from miniep_b200 import Placement
     comm.install(Placement.naive(1, E, world))
     # profiling pass: the global per-expert load of these tokens

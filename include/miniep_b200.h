@@ -206,7 +206,13 @@ int mep_check(mep_ctx* ctx);
  * "timeout_ms" (bound on every cross-rank wait, default 10000),
  * "tc_single_cta" (1 = one CTA per 128-row expert tile instead of CTA pairs),
  * "timeline" (1 = kernels stamp the step timeline read by mep_read_timeline;
- * launches enqueued or captured while it is 0 stamp nothing).
+ * launches enqueued or captured while it is 0 stamp nothing),
+ * "dispatch_per_warp" (1, default = one warp places each token; 0 = the
+ * streaming dispatch engine), "router_no_tc" (1 = the warp router even for
+ * batches the tcgen05 router covers), "ffn_ast" (1 = A-stationary GEMM2 for
+ * CTA pairs), "ffn_prefetch" (1 = the expert GEMMs prefetch their next
+ * tile's activation rows into L2). "ffn_ast" and "ffn_prefetch" default to
+ * 0: both measured slower on the bench workload and stay for experiments.
  */
 int mep_set_option(mep_ctx* ctx, const char* name, int64_t value);
 

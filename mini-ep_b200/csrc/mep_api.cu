@@ -45,7 +45,8 @@ struct mep_ctx {
   int tc_single_cta = 0;
   int dispatch_per_warp = 1;  // 0: the streaming engine (k_dispatch_stream) instead of one warp per token
   int router_no_tc = 0;       // 1: never the tcgen05 router
-  int ffn_no_ast = 0;         // 1: GEMM2 without the A-stationary variant
+  int ffn_ast = 0;            // 1: A-stationary GEMM2 (measured slower: a shallower B ring)
+  int ffn_prefetch = 0;       // 1: the GEMMs prefetch their next tile's A rows into L2 (measured slower)
   std::vector<int> placed, n_local_l;
   int cur_layer = -1, stage = 0;
   int64_t cur_n = 0;
@@ -435,7 +436,8 @@ int mep_expert_ffn(mep_ctx* c, const void* w_in, const void* w_out, int n_local,
   a.num_sms = c->num_sms;
   a.force_simt = c->force_simt;
   a.tc_single_cta = c->tc_single_cta;
-  a.no_ast = c->ffn_no_ast;
+  a.ast = c->ffn_ast;
+  a.prefetch = c->ffn_prefetch;
   a.n_local_weights = n_local;
   a.err = c->err_dev;
   a.tl = tl_of(c);
@@ -587,8 +589,12 @@ int mep_set_option(mep_ctx* c, const char* name, int64_t value) {
     c->tc_single_cta = value != 0;
     return MEP_OK;
   }
-  if (!std::strcmp(name, "ffn_no_ast")) {
-    c->ffn_no_ast = value != 0;
+  if (!std::strcmp(name, "ffn_ast")) {
+    c->ffn_ast = value != 0;
+    return MEP_OK;
+  }
+  if (!std::strcmp(name, "ffn_prefetch")) {
+    c->ffn_prefetch = value != 0;
     return MEP_OK;
   }
   if (!std::strcmp(name, "router_no_tc")) {

@@ -308,6 +308,7 @@ struct TcArgs {
   const uint32_t* seq;
   int* err;
   uint64_t* tl;            // step timeline or null
+  int prefetch;            // 1: prefetch the unit's next tile's A rows into L2
 };
 
 // MODE 0: GEMM1 + SwiGLU -> act. MODE 1: GEMM2 -> source landing rows.
@@ -409,6 +410,14 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
         const int arow = c.row0 + (int)cta * 128;
         const int brow = c.j * args.b_rows_per_expert + c.nb * args.b_step;
         const uint32_t a_ph = (uint32_t)(i / args.ntiles_n) & 1u;  // AST: row tiles so far
+        // the rows of this unit's next tile, prefetched into L2 one k-block at a time
+        int next_arow = -1;
+        if (!AST && args.prefetch) {
+          const int tn = unit_tile<AST>(i + 1, unit, nunits, args.ntiles_n);
+          if (tn < total)
+            next_arow = decode_tile(tn, args.ntiles_n, 1, G::TILE_M, G::TILE_M, S->n_local,
+                                    S->prefix, S->base, S->rows).row0 + (int)cta * 128;
+        }
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (AST && c.nb == 0) {
@@ -438,6 +447,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
             tma_load_2d<PAIR>(st + A_TILE, &tmB, kb * BK, brow, bar);
             tma_load_2d<PAIR>(st + A_TILE + A_TILE, &tmB, kb * BK, brow + args.b_second, bar);
           }
+          if (next_arow >= 0) tma_prefetch_2d(&tmA, kb * BK, next_arow);
           if (++s == G::STAGES) {
             s = 0;
             ph ^= 1u;
@@ -719,6 +729,7 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g1.act_ld = I;
     g1.err = a.err;
     g1.tl = a.tl;
+    g1.prefetch = a.prefetch;
     const bool pair = !a.tc_single_cta && a.num_sms >= 2;
     // CTA pairs: 2-CTA clusters over an even grid; single CTAs: one per SM
     // GEMM2's tile stores: every rank's return buffer (ranks past world: unused)
@@ -763,8 +774,9 @@ int launch_ffn(const FfnArgs& a, cudaStream_t st) {
     g2.seq = a.seq;
     g2.err = a.err;
     g2.tl = a.tl;
+    g2.prefetch = a.prefetch;
     // A-stationary GEMM2 when a row tile's A (K = I columns) fits the resident slots
-    const bool ast = pair && !a.no_ast && I / ffn::BK <= ffn::AST_SLOTS;
+    const bool ast = pair && a.ast && I / ffn::BK <= ffn::AST_SLOTS;
     if (ast)
       e = launch(ffn::k_ffn_tc<1, true, true>, true, tmA2, tmB2, g2,
                  ffn::smem_bytes<true, true>());

@@ -174,7 +174,8 @@ struct FfnArgs {
   int num_sms;
   int force_simt;           // 1: run the CUDA-core kernels even for bf16
   int tc_single_cta;        // 1: one CTA per 128x256 tile instead of CTA pairs per 256x256
-  int no_ast;               // 1: GEMM2 reloads A per N block (no A-stationary variant)
+  int ast;                  // 1: GEMM2 keeps a row tile's A resident across its N blocks
+  int prefetch;             // 1: the GEMMs prefetch their next tile's A rows into L2
   int n_local_weights;      // leading extent of w_in / w_out
   int* err;                 // host-mapped device error word
   uint64_t* tl;             // step timeline or null

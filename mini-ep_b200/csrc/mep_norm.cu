@@ -36,14 +36,24 @@ __global__ void __launch_bounds__(256) k_rmsnorm(int64_t n, int H, const T* __re
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const uint32_t u[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+    if (sizeof(T) == 2) {
+      // squares rounded to bf16 two at a time (a bf16x2 multiply rounds the
+      // exact product, as the fp32 multiply and round would), summed in
+      // element order
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-      float e;
-      if (sizeof(T) == 2)
-        e = (j & 1) ? bf16_bits_hi(u[j >> 1]) : bf16_bits_lo(u[j >> 1]);
-      else
-        e = __uint_as_float(u[j]);
-      ss += Elt<T>::round(e * e);
+      for (int q = 0; q < 4; ++q) {
+        const __nv_bfloat162 e2 = *reinterpret_cast<const __nv_bfloat162*>(&u[q]);
+        const __nv_bfloat162 sq = __hmul2(e2, e2);
+        const uint32_t sw = *reinterpret_cast<const uint32_t*>(&sq);
+        ss += bf16_bits_lo(sw);
+        ss += bf16_bits_hi(sw);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const float e = __uint_as_float(u[j]);
+        ss += e * e;
+      }
     }
   }
 #pragma unroll
@@ -59,11 +69,13 @@ __global__ void __launch_bounds__(256) k_rmsnorm(int64_t n, int H, const T* __re
     const uint32_t hu[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
     uint32_t o[4];
     if (sizeof(T) == 2) {
+      // bf16(w * bf16(h * r)), two elements per bf16x2 multiply (r is a bf16
+      // value, so every product is rounded once from its exact value)
+      const __nv_bfloat162 r2 = __float2bfloat162_rn(r);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const float a = Elt<T>::round(bf16_bits_lo(wu[q]) * Elt<T>::round(bf16_bits_lo(hu[q]) * r));
-        const float b = Elt<T>::round(bf16_bits_hi(wu[q]) * Elt<T>::round(bf16_bits_hi(hu[q]) * r));
-        const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+        const __nv_bfloat162 hn = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&hu[q]), r2);
+        const __nv_bfloat162 p = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&wu[q]), hn);
         o[q] = *reinterpret_cast<const uint32_t*>(&p);
       }
     } else {

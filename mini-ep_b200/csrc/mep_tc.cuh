@@ -27,6 +27,14 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Prefetch a 2D tile into L2 (no shared memory, no barrier): a later TMA
+// load of it then waits for L2 rather than DRAM.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* tm, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(x), "r"(y)
+               : "memory");
+}
 // 2D TMA tile load into this CTA's shared memory. Single CTA: completes on
 // this CTA's barrier. Pair: completes on the pair leader's barrier, given as
 // a shared::cluster address.

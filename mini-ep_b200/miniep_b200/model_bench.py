@@ -3,12 +3,13 @@ a 24-layer Granite-3.0-1B-A400M-shaped decoder with synthetic weights, every
 MoE layer on the expert-parallel CUDA layer, one process per GPU.
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 \\
-        -m miniep_b200.model_bench --config 2 [--plan naive|balanced]
+        -m miniep_b200.model_bench --config 2 [--plan naive|balanced|lpt]
 
   config 2: prefill 8 sequences x 256 random token ids, 32 greedy steps
   config 3: 16 x 512 prefill, 32 greedy steps, Zipf(1.2) router bias per layer;
-            run under naive placement, then the balancer's plan from the first
-            run's route counts (2 slots per rank): continuations must be identical
+            run under naive placement, then the balancer's plan and the LPT plan
+            from the first run's route counts (2 slots per rank): continuations
+            must be identical across the three
   config 4: 64 sequences over a 1024-token random context, 128 decode steps of
             one token per sequence; reports the latency per decode step
 
@@ -27,7 +28,7 @@ import time
 import torch
 import torch.distributed as dist
 
-from . import Comm, EPMoEBackend, EPStats, Placement, plan_balanced, synth
+from . import Comm, EPMoEBackend, EPStats, Placement, plan_balanced, plan_lpt, synth
 from .model import (GRANITE_1B_A400M, DeviceModel, Engine, ModelConfig, Shard,
                     expert_weight_keys, random_weights)
 
@@ -116,7 +117,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--layers", type=int, default=24)
-    ap.add_argument("--plan", choices=["naive", "balanced"], default="naive")
+    ap.add_argument("--plan", choices=["naive", "balanced", "lpt"], default="naive",
+                    help="placement re-planned from the naive run's counts (config 3 runs both)")
     ap.add_argument("--eager-decode", action="store_true",
                     help="launch each decode step op by op instead of one graph replay")
     a = ap.parse_args()
@@ -134,12 +136,16 @@ def main():
     graphed = not a.eager_decode
     res = _run(cfg, w, naive, prompts, c["new"], biases, rank, local, graphed)
     runs = {"naive": res}
-    if a.config == 3 or a.plan == "balanced":
+    wanted = ["balanced", "lpt"] if a.config == 3 else [a.plan]
+    wanted = [p for p in wanted if p != "naive"]
+    if wanted:
         counts = res["route_counts"].cuda()
         if world > 1:
             dist.all_reduce(counts)
-        plan, _ = plan_balanced(counts.cpu(), world, slots_per_rank=2)
-        runs["balanced"] = _run(cfg, w, plan, prompts, c["new"], biases, rank, local, graphed)
+    for name in wanted:
+        planner = plan_balanced if name == "balanced" else plan_lpt
+        plan, _ = planner(counts.cpu(), world, slots_per_rank=2)
+        runs[name] = _run(cfg, w, plan, prompts, c["new"], biases, rank, local, graphed)
     # whole-job figures: positions summed, wall time max over ranks
     out = {}
     for name, r in runs.items():
@@ -152,9 +158,9 @@ def main():
             t[0] = pos[0]
         out[name] = t.tolist()
     same = None
-    if "balanced" in runs:
-        flag = torch.tensor([int(runs["naive"]["generated"] == runs["balanced"]["generated"])],
-                            device="cuda")
+    if len(runs) > 1:
+        flag = torch.tensor([int(all(r["generated"] == runs["naive"]["generated"]
+                                     for r in runs.values()))], device="cuda")
         if world > 1:
             dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         same = bool(flag.item())
@@ -167,7 +173,7 @@ def main():
             line[name] = {"tok_pos_per_s": pos / wall, "positions": int(pos), "wall_s": wall,
                           "prefill_s": pre, "decode_ms_per_step": dec / c["new"] * 1e3}
         if same is not None:
-            line["greedy_identical_naive_vs_balanced"] = same
+            line["greedy_identical_across_plans"] = same
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
