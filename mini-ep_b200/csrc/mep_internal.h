@@ -94,7 +94,7 @@ struct WaitCfg {
 // `tl` (every launcher below that takes it): the step timeline, or null when
 // the context's timeline option is off (mep_device.cuh, tl_begin / tl_end)
 // use_tc: allow the tcgen05 router from kRouterTcMinTokens tokens
-constexpr int64_t kRouterTcMinTokens = 4096;
+constexpr int64_t kRouterTcMinTokens = 256;
 void launch_router(int dtype, const void* x, const void* router_w, const float* bias,
                    int64_t n, int hidden, int experts, int topk, int64_t* idx_out,
                    void* gate_out, float* logits_out, int num_sms, int use_tc, int* err,

@@ -1,6 +1,6 @@
 // Router on the tcgen05 tensor cores, for large token counts (bf16, E = 32 or
-// 64 experts): logits = x @ router^T (miniep/modeling.py:193) per 128-token
-// tile, one tcgen05.mma chain (M = 128 tokens, N = E, K = 16 per
+// 64 experts): logits = x @ router^T (miniep/modeling.py:193) per tile of up
+// to 128 tokens, one tcgen05.mma chain (M = 128 rows, N = E, K = 16 per
 // instruction) over TMA-loaded, 128B-swizzled K-slices of x and of the
 // router rows, accumulated in TMEM in fp32 (double-buffered, so the next
 // tile accumulates while this one is selected). One epilogue thread per
@@ -10,7 +10,9 @@
 // router's selection, so both give the same indices and gates for the same
 // logits.
 //
-// Persistent: one CTA per SM walks the tiles. Warp 0 issues the TMA loads
+// Persistent: one CTA per SM walks the tiles, sized so that every SM gets one
+// (a tile of tpt < 128 tokens loads tpt rows; the MMA's other rows are
+// dropped). Warp 0 issues the TMA loads
 // into an 8-stage ring, warp 1 the MMAs, warps 2-5 (one per TMEM lane
 // quadrant) drain the accumulator. Every mbarrier wait is bounded.
 #include <cmath>
@@ -60,6 +62,7 @@ constexpr int smem_bytes() {
 struct RouterArgs {
   int64_t n;
   int H, k;
+  int tpt;  // tokens per tile (<= TILE): the grid covers every SM even when n < TILE * SMs
   const float* bias;
   int64_t* idx_out;
   bf16* gate_out;
@@ -97,7 +100,6 @@ __global__ void __launch_bounds__(THREADS, 1) k_router_tc(const __grid_constant_
     S->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  for (int e = threadIdx.x; e < E; e += blockDim.x) S->bias[e] = a.bias ? a.bias[e] : 0.f;
   if (wp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&S->tmem_base)),
@@ -105,11 +107,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_router_tc(const __grid_constant_
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  for (int e = threadIdx.x; e < E; e += blockDim.x) S->bias[e] = a.bias ? a.bias[e] : 0.f;
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = S->tmem_base;
-  const int ntiles = (int)((a.n + TILE - 1) / TILE);
+  const int ntiles = (int)((a.n + a.tpt - 1) / a.tpt);
   const int kblocks = a.H / BK;
 
   if (wp == 0) {
@@ -124,9 +127,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_router_tc(const __grid_constant_
             ok = false;
             break;
           }
-          mbar_expect_tx(&S->full[s], (uint32_t)C::STAGE);
+          mbar_expect_tx(&S->full[s], (uint32_t)(a.tpt * BK * 2 + C::B_BYTES));
           uint8_t* st = smem + s * C::STAGE;
-          tma_load_2d<false>(st, &tmX, kb * BK, t * TILE, smem_u32(&S->full[s]));
+          tma_load_2d<false>(st, &tmX, kb * BK, t * a.tpt, smem_u32(&S->full[s]));
           tma_load_2d<false>(st + C::A_BYTES, &tmW, kb * BK, 0, smem_u32(&S->full[s]));
           if (++s == STAGES) {
             s = 0;
@@ -189,8 +192,11 @@ __global__ void __launch_bounds__(THREADS, 1) k_router_tc(const __grid_constant_
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S->tempty[b]);
-      const int64_t tok = (int64_t)t * TILE + q * 32 + lane;
-      if (tok >= a.n) continue;
+      // accumulator rows at or past tpt come from shared memory the tile's
+      // load did not write: they are computed and dropped
+      const int row = q * 32 + lane;
+      const int64_t tok = (int64_t)t * a.tpt + row;
+      if (row >= a.tpt || tok >= a.n) continue;
       float v[E];
 #pragma unroll
       for (int e = 0; e < E; ++e) {
@@ -262,11 +268,17 @@ int launch(int64_t n, int hidden, int topk, const void* x, const void* router_w,
       return -1;
     attr_set = true;
   }
+  // tiles of tpt tokens (a multiple of 8, the swizzle atom's rows): enough
+  // tiles for every SM, at most TILE tokens each
+  int64_t tpt = (n + num_sms - 1) / num_sms;
+  tpt = (tpt + 7) / 8 * 8;
+  if (tpt > TILE) tpt = TILE;
   CUtensorMap tmX, tmW;
-  if (encode_bf16_2d(&tmX, x, (uint64_t)hidden, (uint64_t)n, BK, TILE)) return -1;
+  if (encode_bf16_2d(&tmX, x, (uint64_t)hidden, (uint64_t)n, BK, (uint32_t)tpt)) return -1;
   if (encode_bf16_2d(&tmW, router_w, (uint64_t)hidden, (uint64_t)E, BK, E)) return -1;
-  RouterArgs a{n, hidden, topk, bias, idx_out, static_cast<bf16*>(gate_out), logits_out, err, tl};
-  const int64_t ntiles = (n + TILE - 1) / TILE;
+  RouterArgs a{n, hidden, topk, (int)tpt, bias, idx_out, static_cast<bf16*>(gate_out),
+               logits_out, err, tl};
+  const int64_t ntiles = (n + tpt - 1) / tpt;
   const unsigned grid = (unsigned)(ntiles < num_sms ? ntiles : num_sms);
   k_router_tc<E><<<grid, THREADS, smem_bytes<E>(), st>>>(tmX, tmW, a);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;

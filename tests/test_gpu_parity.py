@@ -79,7 +79,7 @@ def test_router_fp32_config1(golden):
                           rtol=1e-5, atol=1e-6)
 
 
-# 4096 and more tokens take the tcgen05 router, fewer the warp-level kernel
+# 256 and more tokens take the tcgen05 router, fewer the warp-level kernel
 @pytest.mark.parametrize("shape,n", [("a", 4096), ("a", 1), ("a", 1000), ("b", 1024), ("b", 33),
                                      ("b", 4100), ("a", 20000)])
 def test_router_bf16_skewed(shape, n):
@@ -120,13 +120,13 @@ def test_router_bf16_skewed(shape, n):
           f"rounding-moved rows {int(off.sum())} of {int((~ties).sum())} tie-free")
 
 
-@pytest.mark.parametrize("shape", ["a", "b"])
-def test_router_tcgen05_and_warp_kernels_agree(shape):
-    """The tcgen05 router (large batches) and the warp-level kernel select
-    the same experts and gates wherever their fp32 sums round to the same
-    bf16 logits, and their logits differ by at most one rounding step."""
+@pytest.mark.parametrize("shape,n", [("a", 8192), ("b", 8192), ("a", 2048), ("b", 300)])
+def test_router_tcgen05_and_warp_kernels_agree(shape, n):
+    """The tcgen05 router and the warp-level kernel select the same experts
+    and gates wherever their fp32 sums round to the same bf16 logits, and
+    their logits differ by at most one rounding step (the tcgen05 kernel's
+    tiles hold 56 tokens at 8192, 16 at 2048 and 8 at 300 on 148 SMs)."""
     sh = synth.SHAPES[shape]
-    n = 8192
     lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=5, dtype=torch.bfloat16)
     bias = synth.zipf_router_bias(1, sh["experts"])[0].cuda()
     comm = world1_comm(sh["experts"], sh["topk"], sh["hidden"], sh["inter"], n, torch.bfloat16)
