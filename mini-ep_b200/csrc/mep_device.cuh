@@ -142,6 +142,16 @@ __device__ __forceinline__ void bulk_store_s2g(void* dst, const void* src, uint3
                : "memory");
 }
 
+// inclusive prefix sum over the 32 lanes of a warp
+__device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 

@@ -33,6 +33,7 @@ using bf16 = __nv_bfloat16;
 
 __device__ __forceinline__ void grid_done_signal_ffn(unsigned int* done_ctr, const PeerPtrs& peers,
                                                      int world, int rank, const uint32_t* seq) {
+  if (world == 1) return;  // one rank: the combine follows in stream order
   __syncthreads();  // this CTA's stores happen before thread 0's fence below
   if (threadIdx.x == 0) {
     __threadfence_system();
@@ -338,6 +339,12 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
   const bool leader = cta == 0;
   tl_begin(args.tl, MODE == 0 ? kTlGemm1 : kTlGemm2);
 
+  if (threadIdx.x == 32) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (MODE == 1)
+      for (int r = 0; r < args.world; ++r) tma_prefetch_desc(&rmaps.m[r]);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < G::STAGES; ++s) {
       mbar_init(&S->full[s], 1);
@@ -370,21 +377,28 @@ __global__ void __launch_bounds__(THREADS, 1) k_ffn_tc(const __grid_constant__ C
     }
   }
   {
+    // the local segments, loaded in parallel; warp 2 scans their row tiles
+    // of TILE_M rows (one load round trip, not one per expert)
     const Layout* lay = args.lay;
     const int nl = lay->n_local;
-    if (threadIdx.x == 0) {
-      int tiles = 0;  // row tiles of TILE_M rows per local expert
-      for (int j = 0; j < nl; ++j) {
-        S->prefix[j] = tiles;
-        tiles += (lay->seg_rows[j] + G::TILE_M - 1) / G::TILE_M;
-      }
-      S->prefix[nl] = tiles;
-      S->n_local = nl;
-      S->total = lay->total_mtiles > 0 ? tiles * args.ntiles_n : 0;
-    }
     for (int i = threadIdx.x; i < nl; i += blockDim.x) {
       S->base[i] = lay->seg_base[i];
       S->rows[i] = lay->seg_rows[i];
+    }
+    if (wp == 2) {
+      int run = 0;
+      for (int j0 = 0; j0 < nl; j0 += 32) {
+        const int j = j0 + lane;
+        const int t = j < nl ? (lay->seg_rows[j] + G::TILE_M - 1) / G::TILE_M : 0;
+        const int inc = warp_inclusive_scan(t, lane);
+        if (j < nl) S->prefix[j] = run + inc - t;
+        run += __shfl_sync(0xffffffffu, inc, 31);
+      }
+      if (lane == 0) {
+        S->prefix[nl] = run;
+        S->n_local = nl;
+        S->total = lay->total_mtiles > 0 ? run * args.ntiles_n : 0;
+      }
     }
   }
   fence_before();

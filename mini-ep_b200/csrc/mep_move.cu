@@ -27,6 +27,7 @@ using bf16 = __nv_bfloat16;
 __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const PeerPtrs& peers,
                                                  int world, int rank, int flag_base,
                                                  const uint32_t* seq) {
+  if (world == 1) return;  // one rank: the next kernels follow in stream order
   __syncthreads();  // this CTA's stores happen before thread 0's fence below
   if (threadIdx.x == 0) {
     __threadfence_system();
@@ -442,7 +443,9 @@ __device__ __forceinline__ void combine_body(int64_t n, int topk, int H, int wor
                                              WaitCfg wc, uint64_t* tl) {
   constexpr int V = Vec16<T>::N;
   tl_begin(tl, kTlCombine);
-  if (threadIdx.x < world) wait_flag(flags + 2 * world + threadIdx.x, *seq, kErrWaitDone, wc);
+  // expert outputs from every rank (one rank: GEMM2 precedes in stream order)
+  if (world > 1 && threadIdx.x < world)
+    wait_flag(flags + 2 * world + threadIdx.x, *seq, kErrWaitDone, wc);
   __syncthreads();
   tl_begin(tl, kTlResultsIn);
   const int lane = lane_id();

@@ -25,11 +25,14 @@ constexpr int kRouteThreads = kRouteChunkTokens;  // one token per thread in the
 constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kRoutePrefetch = 8;  // independent loads a thread keeps in flight
 
+// the token of entry f: a 64-bit division, kept out of line so that the
+// unrolled scans that never need it (no valid mask) stay short
+__device__ __noinline__ int64_t entry_token(int64_t f, int k) { return f / k; }
+
 __device__ __forceinline__ int entry_expert(const int64_t* idx, const uint8_t* valid, int64_t f,
                                             int k, int64_t n, int E, int* err) {
-  const int64_t t = f / k;
-  if (t >= n) return -1;
-  if (valid && !valid[t]) return -1;
+  if (f >= n * k) return -1;
+  if (valid && !valid[entry_token(f, k)]) return -1;
   const int64_t e = idx[f];
   if (e < 0 || e >= E) {
     set_err(err, kErrExpertId);
@@ -151,15 +154,6 @@ __global__ void __launch_bounds__(256) k_route_rr_advance(int nchunks, int E,
     for (int ch = 0; ch < nchunks; ++ch) c += chunk_hist[(int64_t)ch * E + e];
     rr[e] += c;
   }
-}
-
-__device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int t = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += t;
-  }
-  return v;
 }
 
 // Receive layout, send offsets and return-buffer tables from the exchanged
@@ -477,7 +471,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     }
     // the receive layout, once every rank's counts are in
     extern __shared__ int route_dyn[];  // world * world * E counts for the layout pass
-    layout_block(world, rank, E, owners, nrep, cnt_in, flags, recv_per_layer, cap_rows, lay,
+    layout_block(world, rank, E, s_own, s_nrep, cnt_in, flags, recv_per_layer, cap_rows, lay,
                  step, wc, route_dyn);
     __syncthreads();
     if (threadIdx.x == 0) tl_mark(tl, kTlLayout);
@@ -527,9 +521,13 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
       if (e >= 0) {
         const int within = base[e] + wbase[wp][e] + wcnt[wp][e] + rank_in_round;
         const int nr = s_nrep[e];
-        const int slot = (rr_mod[e] + within) % nr;
+        int slot = 0;
+        grp = within;
+        if (nr > 1) {  // a replicated expert: round-robin over its owners
+          slot = (rr_mod[e] + within) % nr;
+          grp = within / nr;
+        }
         dest = s_own[e * kMaxWorld + slot];
-        grp = within / nr;
       }
       __syncwarp();
       if (e >= 0 && rank_in_round == 0) wcnt[wp][e] += __popc(peers_mask);

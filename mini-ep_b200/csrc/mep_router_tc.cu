@@ -88,6 +88,10 @@ __global__ void __launch_bounds__(THREADS, 1) k_router_tc(const __grid_constant_
   Smem* S = reinterpret_cast<Smem*>(smem + C::DATA);
   const int wp = warp_id(), lane = lane_id();
   tl_begin(a.tl, kTlRouter);
+  if (threadIdx.x == 32) {
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&S->full[s], 1);

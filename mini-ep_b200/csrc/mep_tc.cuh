@@ -27,6 +27,12 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Fetch a tensor map (a __grid_constant__ kernel parameter) into the
+// descriptor cache, so the first TMA copy that names it does not wait for it.
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+
 // Prefetch a 2D tile into L2 (no shared memory, no barrier): a later TMA
 // load of it then waits for L2 rather than DRAM.
 __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* tm, int x, int y) {
