@@ -340,6 +340,8 @@ __device__ __forceinline__ bool grid_barrier(RouteSync* gs, unsigned nblocks, co
   return ok != 0;
 }
 
+static_assert(kMaxExperts <= 128, "the ranking keeps expert ids as int8");
+
 __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     int64_t n, int k, int E, int64_t tpc, int world, int rank, const int64_t* __restrict__ idx,
     const uint8_t* __restrict__ valid, const int32_t* __restrict__ owners,
@@ -354,6 +356,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
   __shared__ int rr_mod[kMaxExperts];
   __shared__ int wcnt[kRouteWarps][kMaxExperts];
   __shared__ int wbase[kRouteWarps][kMaxExperts];
+  __shared__ int8_t s_ev[kRouteWarps][kMaxTopk][32];  // a round's entries: expert id or -1
   __shared__ int cnt[kMaxWorld * kMaxExperts];
   __shared__ int s_nrep[kMaxExperts];
   __shared__ int s_own[kMaxExperts * kMaxWorld];
@@ -377,10 +380,11 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     rr_mod[e] = (int)(((rr[e] % nr) + nr) % nr);  // >= 0 for any rr
   }
   for (int i = threadIdx.x; i < E * kMaxWorld; i += blockDim.x) s_own[i] = owners[i];
+  for (int i = threadIdx.x; i < kRouteWarps * kMaxExperts; i += blockDim.x) (&wcnt[0][0])[i] = 0;
   __syncthreads();
-  // lanes holding the same expert add once (skewed routing piles entries on
-  // a few experts, so one shared counter would take most of the atomics);
-  // each thread keeps kRoutePrefetch loads in flight
+  // per-warp counters, and lanes holding the same expert add once: no
+  // atomics (skewed routing piles entries on a few experts); each thread
+  // keeps kRoutePrefetch loads in flight
   const unsigned lt_mask = (1u << lane) - 1u;
   for (int64_t f0 = t_beg * k; f0 < t_end * k; f0 += (int64_t)blockDim.x * kRoutePrefetch) {
     int ev[kRoutePrefetch];
@@ -392,11 +396,16 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
 #pragma unroll
     for (int j = 0; j < kRoutePrefetch; ++j) {
       const unsigned same = __match_any_sync(0xffffffffu, ev[j]);
-      if (ev[j] >= 0 && (same & lt_mask) == 0) atomicAdd(&hist[ev[j]], __popc(same));
+      if (ev[j] >= 0 && (same & lt_mask) == 0) wcnt[wp][ev[j]] += __popc(same);
     }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_hist[(int64_t)b * E + e] = hist[e];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int c = 0;
+    for (int w = 0; w < kRouteWarps; ++w) c += wcnt[w][e];
+    hist[e] = c;
+    chunk_hist[(int64_t)b * E + e] = c;
+  }
   tl_end(tl, kTlRouteHist);
   if (!grid_barrier(gs, gridDim.x, wc)) {
     // the barrier timed out (error word set): another CTA's histogram may be
@@ -485,17 +494,19 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
     const int64_t t0 = r0 + wp * 32;
     const int64_t f0 = t0 * k;
     const int64_t f_end = min(r0 + kRouteChunkTokens, t_end) * k;
-    // this warp's entries of the round, loaded once for both passes
-    int ev[kMaxTopk];
-#pragma unroll
-    for (int r = 0; r < kMaxTopk; ++r) {
+    // this warp's entries of the round, loaded once for both passes into
+    // shared memory. The loops stay rolled: each CTA runs them once or a few
+    // times, so their time is the instruction fetch of their code, not its
+    // issue.
+#pragma unroll 1
+    for (int r = 0; r < k; ++r) {
       const int64_t f = f0 + r * 32 + lane;
-      ev[r] = (r < k && f < f_end) ? entry_expert(idx, valid, f, k, n, E, nullptr) : -1;
+      s_ev[wp][r][lane] = f < f_end ? entry_expert(idx, valid, f, k, n, E, nullptr) : -1;
     }
-#pragma unroll
-    for (int r = 0; r < kMaxTopk; ++r) {
-      if (r >= k) break;
-      const int e = ev[r];
+    __syncwarp();
+#pragma unroll 1
+    for (int r = 0; r < k; ++r) {
+      const int e = s_ev[wp][r][lane];
       const unsigned same = __match_any_sync(0xffffffffu, e);
       if (e >= 0 && (same & lt_mask) == 0) wcnt[wp][e] += __popc(same);
     }
@@ -510,11 +521,10 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
       hist[e] = run;  // this round's total, added to base after the pass
     }
     __syncthreads();
-#pragma unroll
-    for (int r = 0; r < kMaxTopk; ++r) {
-      if (r >= k) break;
+#pragma unroll 1
+    for (int r = 0; r < k; ++r) {
       const int64_t f = f0 + r * 32 + lane;
-      const int e = ev[r];
+      const int e = s_ev[wp][r][lane];
       const unsigned peers_mask = __match_any_sync(0xffffffffu, e);
       const int rank_in_round = __popc(peers_mask & lt_mask);
       int dest = -1, grp = 0;
