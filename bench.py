@@ -611,8 +611,9 @@ def main_b200(a):
             "recv_rows_per_rank": [r["recv_rows"] for r in got],
             "wall_s_timed_region": wall,
             # per step: norm, router, routing, dispatch, gemm1, gemm2, combine
-            # (+ data wait and fan-out, and the step-start rank barrier, when N > 1)
-            "gpu_launches": (7 + 3 * (world > 1)) * a.steps,
+            # (+ the fan-out, which waits for the peers' rows, and the step-start
+            # rank barrier, when N > 1)
+            "gpu_launches": (7 + 2 * (world > 1)) * a.steps,
             "clocks": clk,
         }
         if remote is not None:

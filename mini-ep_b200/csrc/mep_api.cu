@@ -34,7 +34,7 @@ struct mep_ctx {
   int64_t* rr = nullptr;      // [L][E]
   int64_t* route_counts = nullptr;    // [L][E]
   int64_t* recv_per_layer = nullptr;  // [L]
-  unsigned int* done_ctr = nullptr;   // [0] dispatch, [1] expert FFN, [2..3] routing grid barrier
+  unsigned int* done_ctr = nullptr;   // kDoneCounters completion counters (mep_internal.h)
   int* err_host = nullptr;
   int* err_dev = nullptr;
   uint32_t* seq = nullptr;  // device: sequence number of the current layer step
@@ -218,7 +218,7 @@ int mep_ctx_create(int rank, int world, int device, int num_layers, int num_expe
       {reinterpret_cast<void**>(&c->rr), (size_t)num_layers * num_experts * 8},
       {reinterpret_cast<void**>(&c->route_counts), (size_t)num_layers * num_experts * 8},
       {reinterpret_cast<void**>(&c->recv_per_layer), (size_t)num_layers * 8},
-      {reinterpret_cast<void**>(&c->done_ctr), 4 * sizeof(unsigned int)},
+      {reinterpret_cast<void**>(&c->done_ctr), kDoneCounters * sizeof(unsigned int)},
       {reinterpret_cast<void**>(&c->seq), 2 * sizeof(uint32_t)},  // [0] layer step, [1] barrier
       {reinterpret_cast<void**>(&c->tl), (size_t)kTlSlots * sizeof(uint64_t)},
   };
@@ -397,14 +397,11 @@ int mep_dispatch(mep_ctx* c, const void* x, const int64_t* topk_idx, int64_t n, 
                   c->dispatch_per_warp, c->err_dev, tl_of(c), as_stream(stream));
   // the stage ends when every rank's rows for this rank have landed and sit in
   // their expert-segment rows (one rank: stream order already says so)
-  if (c->world > 1) {
-    launch_wait_flags(reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->world,
-                      c->world, c->seq, 0u, kErrWaitData, wait_cfg(c), tl_of(c), kTlDataIn,
-                      as_stream(stream));
-    launch_fanout(c->dtype, c->H, c->k, c->rank, c->max_tokens, c->layout,
+  if (c->world > 1)
+    launch_fanout(c->dtype, c->H, c->k, c->rank, c->world, c->max_tokens, c->layout,
                   reinterpret_cast<const int32_t*>(c->sym + c->off_meta), c->sym + c->off_land,
-                  c->recv_x, c->num_sms, tl_of(c), as_stream(stream));
-  }
+                  c->recv_x, reinterpret_cast<const uint32_t*>(c->sym + c->off_flags), c->seq,
+                  wait_cfg(c), c->num_sms, tl_of(c), as_stream(stream));
   MEP_CK(c, cudaGetLastError());
   c->stage = 2;
   return MEP_OK;

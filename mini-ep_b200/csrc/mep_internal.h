@@ -16,6 +16,13 @@ constexpr int kMaxExperts = 128;  // experts per layer
 constexpr int kMaxTopk = 16;
 constexpr int kRowAlign = 128;    // expert segments in the receive buffer start on 128-row boundaries
 constexpr int kRouteChunkTokens = 256;  // tokens per CTA in the routing scan
+// completion counters of a context: [0] dispatch, [1] expert FFN, [2..3]
+// routing grid barrier; from kDoneGroupBase, kDoneGroups dispatch group
+// counters, one per 128-byte line (kDoneGroupStride words apart)
+constexpr int kDoneGroups = 32;
+constexpr int kDoneGroupBase = 32;
+constexpr int kDoneGroupStride = 32;
+constexpr int kDoneCounters = kDoneGroupBase + kDoneGroups * kDoneGroupStride;
 
 enum DType : int { kF32 = 0, kBF16 = 1 };
 
@@ -139,11 +146,13 @@ void launch_rank_barrier(const PeerPtrs& peers, int world, int rank, uint32_t* b
                          const uint32_t* flags_local, WaitCfg wc, uint64_t* tl, cudaStream_t st);
 
 // waits for flags [first, first + world) to reach *seq (or `target` when seq is null)
-// Receive rows that came from other ranks: copy each from the landing
-// buffer (row [src][token]) to its expert-segment row.
-void launch_fanout(int dtype, int hidden, int topk, int rank, int64_t max_tokens,
+// Receive rows that came from other ranks: once every rank's data flag for
+// this step is up (bounded wait, timeline mark MEP_TL_DATA_IN), copy each
+// from the landing buffer (row [src][token]) to its expert-segment row.
+void launch_fanout(int dtype, int hidden, int topk, int rank, int world, int64_t max_tokens,
                    const Layout* layout, const int32_t* recv_meta, const void* land,
-                   void* recv_x, int num_sms, uint64_t* tl, cudaStream_t st);
+                   void* recv_x, const uint32_t* flags_local, const uint32_t* seq, WaitCfg wc,
+                   int num_sms, uint64_t* tl, cudaStream_t st);
 
 // `tl_slot`: timeline slot stamped when the wait ends (ignored when tl is null)
 void launch_wait_flags(const uint32_t* flags_local, int first, int world, const uint32_t* seq,

@@ -24,19 +24,29 @@ using bf16 = __nv_bfloat16;
 
 // Signal "this kernel's stores are done" to every rank: flag slot
 // [flag_base + rank] on each peer is raised to `seq` by the last CTA to finish.
+// The CTAs count in kDoneGroups group counters (CTA b in group b % 32, each
+// counter on its own cache line) and the last CTA of each group counts in
+// done_ctr[0], so a grid of thousands of CTAs does not queue on one address.
 __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const PeerPtrs& peers,
                                                  int world, int rank, int flag_base,
                                                  const uint32_t* seq) {
   if (world == 1) return;  // one rank: the next kernels follow in stream order
   __syncthreads();  // this CTA's stores happen before thread 0's fence below
   if (threadIdx.x == 0) {
+    const unsigned grid = gridDim.x, g = blockIdx.x % kDoneGroups;
+    const unsigned members = grid / kDoneGroups + (g < grid % kDoneGroups ? 1u : 0u);
+    const unsigned groups = grid < kDoneGroups ? grid : kDoneGroups;
+    unsigned int* grp = done_ctr + kDoneGroupBase + g * kDoneGroupStride;
     __threadfence_system();
-    const unsigned prev = atomicAdd(done_ctr, 1u);
-    if (prev == gridDim.x - 1) {
-      __threadfence_system();
-      const uint32_t step = *seq;
-      for (int d = 0; d < world; ++d) st_release_sys(peers.flags[d] + flag_base + rank, step);
-      *done_ctr = 0u;
+    if (atomicAdd(grp, 1u) == members - 1) {
+      *grp = 0u;               // the group is complete: reset for the next launch
+      __threadfence_system();  // the group's stores before its count below
+      if (atomicAdd(done_ctr, 1u) == groups - 1) {
+        __threadfence_system();
+        const uint32_t step = *seq;
+        for (int d = 0; d < world; ++d) st_release_sys(peers.flags[d] + flag_base + rank, step);
+        *done_ctr = 0u;
+      }
     }
   }
 }
@@ -303,15 +313,27 @@ __global__ void __launch_bounds__(32 * kDspWarps, 1) k_dispatch_stream(
   tl_end(tl, kTlDispatch + 1);
 }
 
-// Fan-out on the receiver: every receive row whose tag names another rank is
-// copied from that rank's landing row [src][token] (one warp per row).
-__global__ void __launch_bounds__(256) k_fanout(int row_bytes, int topk, int rank,
+// Fan-out on the receiver: once every rank's dispatch has signalled its rows
+// for this rank (data flags [W, 2W), bounded wait), every receive row whose
+// tag names another rank is copied from that rank's landing row
+// [src][token] (one warp per row).
+__global__ void __launch_bounds__(256) k_fanout(int row_bytes, int topk, int rank, int world,
                                                 int64_t max_tokens, const Layout* __restrict__ lay,
                                                 const int32_t* __restrict__ meta,
                                                 const uint8_t* __restrict__ land,
-                                                uint8_t* __restrict__ recv_x, uint64_t* tl) {
+                                                uint8_t* __restrict__ recv_x,
+                                                const uint32_t* flags, const uint32_t* seq,
+                                                WaitCfg wc, uint64_t* tl) {
   __shared__ int s_prefix[kMaxExperts + 1], s_base[kMaxExperts], s_rows[kMaxExperts];
+  __shared__ int arrived;
   tl_begin(tl, kTlFanout);
+  if (threadIdx.x == 0) arrived = 1;
+  __syncthreads();
+  if (threadIdx.x < world && !wait_flag(flags + world + threadIdx.x, *seq, kErrWaitData, wc))
+    arrived = 0;
+  __syncthreads();
+  if (!arrived) return;  // the error word is set; the step fails as a whole
+  if (blockIdx.x == 0 && threadIdx.x == 0) tl_mark(tl, kTlDataIn);
   const int nl = lay->n_local;
   for (int i = threadIdx.x; i <= nl; i += blockDim.x) s_prefix[i] = lay->tile_prefix[i];
   for (int i = threadIdx.x; i < nl; i += blockDim.x) {
@@ -575,13 +597,15 @@ void launch_dispatch(int dtype, int64_t n, int topk, int hidden, int world, int 
       ent_dest, ent_grp, layout, peers, done_ctr, seq, tl);
 }
 
-void launch_fanout(int dtype, int hidden, int topk, int rank, int64_t max_tokens,
+void launch_fanout(int dtype, int hidden, int topk, int rank, int world, int64_t max_tokens,
                    const Layout* layout, const int32_t* recv_meta, const void* land, void* recv_x,
-                   int num_sms, uint64_t* tl, cudaStream_t st) {
+                   const uint32_t* flags_local, const uint32_t* seq, WaitCfg wc, int num_sms,
+                   uint64_t* tl, cudaStream_t st) {
   k_fanout<<<(unsigned)num_sms * 8, 256, 0, st>>>(hidden * (dtype == kBF16 ? 2 : 4), topk, rank,
-                                                  max_tokens, layout, recv_meta,
+                                                  world, max_tokens, layout, recv_meta,
                                                   static_cast<const uint8_t*>(land),
-                                                  static_cast<uint8_t*>(recv_x), tl);
+                                                  static_cast<uint8_t*>(recv_x), flags_local, seq,
+                                                  wc, tl);
 }
 
 void launch_rank_barrier(const PeerPtrs& peers, int world, int rank, uint32_t* bar_seq,

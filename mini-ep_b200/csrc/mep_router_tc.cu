@@ -214,41 +214,34 @@ __global__ void __launch_bounds__(THREADS, 1) k_router_tc(const __grid_constant_
 #pragma unroll
         for (int e = 0; e < E; e += 4) lo[e / 4] = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
       }
-      // top-k: larger value first, the lower expert index on ties
+      // top-k: larger value first, the lower expert index on ties. The
+      // rounds stay rolled (each CTA runs this code for a tile or two, so
+      // its instruction fetch, not its issue, is what costs); the scan over
+      // the E logits is unrolled to keep them in registers.
       unsigned long long used = 0ull;
       float top0 = 0.f, ex_sum = 0.f;
       float ex[kMaxTopk];
-      int sel[kMaxTopk];
+#pragma unroll 1
+      for (int i = 0; i < a.k; ++i) {
+        float best = 0.f;
+        int bi = -1;
 #pragma unroll
-      for (int i = 0; i < kMaxTopk; ++i) {
-        ex[i] = 0.f;
-        sel[i] = 0;
-        if (i < a.k) {
-          float best = 0.f;
-          int bi = -1;
-#pragma unroll
-          for (int e = 0; e < E; ++e) {
-            const bool avail = ((used >> e) & 1ull) == 0ull;
-            if (avail && (bi < 0 || v[e] > best)) {
-              best = v[e];
-              bi = e;
-            }
+        for (int e = 0; e < E; ++e) {
+          const bool avail = ((used >> e) & 1ull) == 0ull;
+          if (avail && (bi < 0 || v[e] > best)) {
+            best = v[e];
+            bi = e;
           }
-          used |= 1ull << bi;
-          if (i == 0) top0 = best;
-          ex[i] = expf(best - top0);
-          ex_sum += ex[i];
-          sel[i] = bi;
         }
+        used |= 1ull << bi;
+        if (i == 0) top0 = best;
+        ex[i] = expf(best - top0);
+        ex_sum += ex[i];
+        a.idx_out[tok * a.k + i] = bi;
       }
       const float rs = 1.f / ex_sum;
-#pragma unroll
-      for (int i = 0; i < kMaxTopk; ++i) {
-        if (i < a.k) {
-          a.idx_out[tok * a.k + i] = sel[i];
-          a.gate_out[tok * a.k + i] = __float2bfloat16_rn(ex[i] * rs);
-        }
-      }
+#pragma unroll 1
+      for (int i = 0; i < a.k; ++i) a.gate_out[tok * a.k + i] = __float2bfloat16_rn(ex[i] * rs);
     }
   }
   fence_before();
