@@ -536,6 +536,30 @@ def main_b200(a):
                        f"{a.e2e_depth} device buffer sets), each step's copy in and copy out "
                        "overlapping the neighbouring steps"
                        + (", one CUDA graph per step" if graphed else "")}
+        # the host link alone: the same copies in and out, overlapped the same
+        # way, with no layer step between them (every rank at once)
+        dbuf = torch.empty_like(h)
+        ci, co = torch.cuda.Stream(), torch.cuda.Stream()
+        if world > 1:
+            dist.barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        ci.wait_stream(torch.cuda.current_stream())
+        co.wait_stream(torch.cuda.current_stream())
+        for _ in range(a.steps):
+            with torch.cuda.stream(ci):
+                dbuf.copy_(h_host, non_blocking=True)
+            with torch.cuda.stream(co):
+                out_host.copy_(h, non_blocking=True)
+        torch.cuda.current_stream().wait_stream(ci)
+        torch.cuda.current_stream().wait_stream(co)
+        c1.record()
+        torch.cuda.synchronize()
+        tc = torch.tensor([c0.elapsed_time(c1) / a.steps], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(tc, op=dist.ReduceOp.MAX)
+        e2e["copies_only_ms_per_step"] = tc.item()
+        del dbuf
         comm.check()
         del sblk
     clk = clocks.stop()
