@@ -86,3 +86,29 @@ def test_step_timeline_stamps_every_stage_in_order():
     assert torch.equal(out_on, out_off)
     comm.check()
     comm.close()
+
+
+@pytest.mark.parametrize("option", ["dispatch_per_warp=0", "ffn_ast=1", "ffn_prefetch=1"])
+@pytest.mark.parametrize("n", [4096, 300])
+def test_step_options_change_no_result(option, n):
+    """The selectable variants move the same bytes and issue the same MMAs
+    in another schedule (streaming dispatch engine, A-stationary GEMM2, L2
+    prefetch of the next tile's rows): the block's output, ids and gates are
+    bit-identical to the default step's."""
+    name, value = option.split("=")
+    sh = synth.SHAPES["a"]
+    lb = synth.make_layer(sh["hidden"], sh["experts"], sh["inter"], n, seed=6,
+                          dtype=torch.bfloat16)
+    be = LocalMoEBackend(lb.w_in.cuda(), lb.w_out.cuda(), max_tokens=n, topk=sh["topk"])
+    comm = be.comm
+    h = synth.make_tokens(n, sh["hidden"], seed=10, dtype=torch.bfloat16).cuda()
+    nw = torch.ones(sh["hidden"], dtype=torch.bfloat16, device="cuda")
+    bias = synth.zipf_router_bias(1, sh["experts"])[0].cuda()
+    args = (h, nw, 1e-6, lb.router.cuda(), synth.GRANITE_RESIDUAL_MULTIPLIER)
+    ref = [t.clone() for t in be.moe_block_from_h(*args, bias=bias)[:3]]
+    comm.set_option(name, int(value))
+    got = [t.clone() for t in be.moe_block_from_h(*args, bias=bias)[:3]]
+    comm.check()
+    for a, b in zip(ref, got):
+        assert torch.equal(a, b)
+    comm.close()
