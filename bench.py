@@ -53,7 +53,28 @@ NVLINK_MEASURED_GBS = 770.0  # peer copy per direction, measured on this pool's 
 # layer step, from one ncu capture of this bench at N=1 (profiles/
 # ffn_tc_shape_a_16k_dram.txt): keyed by (shape, tokens per step)
 FFN_DRAM_BYTES = {("a", 16384): 325.20e6 + 110.93e6 + 163.11e6 + 215.29e6}
+# the algorithmic bytes of that capture's launches (receive rows, act, output
+# rows, all 32 experts' weights): other workloads scale the traffic by it
+FFN_ALG_BYTES = {("a", 16384): 131072 * (2 * 1024 + 2 * 512) * 2.0 + 32 * 3.0 * 1024 * 512 * 2}
 NORM_EPS = 1e-6
+
+
+def ffn_traffic(shape: str, tokens: int, world: int, alg_bytes: float):
+    """DRAM traffic of the FFN stage per step on rank 0: the ncu capture of
+    this workload at one GPU when there is one, else that capture scaled by
+    the ratio of algorithmic bytes (traffic tracked the algorithmic bytes,
+    0.90 of them, in the capture). With several GPUs part of GEMM2's writes
+    go to peers over NVLink, so the scaled figure is an upper bound on the
+    local DRAM traffic."""
+    key = (shape, tokens)
+    if world == 1 and key in FFN_DRAM_BYTES:
+        return FFN_DRAM_BYTES[key], "ncu capture of this workload (profiles/ffn_tc_shape_a_16k_dram.txt)"
+    base = ("a", 16384)
+    if shape != base[0]:
+        return None, "no capture of this shape"
+    return (FFN_DRAM_BYTES[base] * alg_bytes / FFN_ALG_BYTES[base],
+            "1-GPU 16384-token capture scaled by this rank's algorithmic bytes (upper bound "
+            "on local DRAM traffic when N > 1: part of GEMM2's writes go to peers)")
 
 
 def parse():
@@ -609,6 +630,7 @@ def main_b200(a):
         flops_rank0 = recv_rows * 6.0 * H * I  # algorithmic FLOPs of this rank's FFN launch
         n_local_w_bytes = len(mine) * 3.0 * H * I * 2
         achieved = flops_rank0 / (sum(ffn_ms) / n_eager / 1e3) / 1e12
+        alg_bytes = recv_rows * (2 * H + 2 * I) * 2.0 + n_local_w_bytes
         parity, remote = None, None
         if parity_in is not None:
             parity, remote = check_parity(got, placement, w_in_all, w_out_all, router_w.cpu(),
@@ -624,11 +646,10 @@ def main_b200(a):
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "peak_source": peak_src,
                          "flops_per_launch": flops_rank0, "ms_per_launch": sum(ffn_ms) / n_eager,
-                         "traffic": (FFN_DRAM_BYTES.get((a.shape, a.tokens)) if world == 1
-                                     else None),
+                         "traffic": ffn_traffic(a.shape, a.tokens, world, alg_bytes)[0],
                          "traffic_unit": "bytes per launch (dram read + write, ncu)",
-                         "algorithmic_bytes": recv_rows * (2 * H + 2 * I) * 2.0
-                         + n_local_w_bytes},
+                         "traffic_source": ffn_traffic(a.shape, a.tokens, world, alg_bytes)[1],
+                         "algorithmic_bytes": alg_bytes},
             "ffn_ms_per_step_max_rank": ms_ffn,
             "eager": {"value": a.tokens / (ms_eager / 1e3), "ms_per_step": ms_eager,
                       "note": "same kernels launched one by one from Python"},
