@@ -36,12 +36,12 @@ __device__ __forceinline__ void grid_done_signal_ffn(unsigned int* done_ctr, con
   if (world == 1) return;  // one rank: the combine follows in stream order
   __syncthreads();  // this CTA's stores happen before thread 0's fence below
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    fence_acq_rel_sys();
     const unsigned prev = atomicAdd(done_ctr, 1u);
     if (prev == gridDim.x - 1) {
-      __threadfence_system();
+      fence_acq_rel_sys();
       const uint32_t step = *seq;
-      for (int d = 0; d < world; ++d) st_release_sys(peers.flags[d] + 2 * world + rank, step);
+      for (int d = 0; d < world; ++d) st_relaxed_sys(peers.flags[d] + 2 * world + rank, step);
       *done_ctr = 0u;
     }
   }

@@ -37,14 +37,14 @@ __device__ __forceinline__ void grid_done_signal(unsigned int* done_ctr, const P
     const unsigned members = grid / kDoneGroups + (g < grid % kDoneGroups ? 1u : 0u);
     const unsigned groups = grid < kDoneGroups ? grid : kDoneGroups;
     unsigned int* grp = done_ctr + kDoneGroupBase + g * kDoneGroupStride;
-    __threadfence_system();
+    fence_acq_rel_sys();  // this CTA's stores (peers' rows included) before its count
     if (atomicAdd(grp, 1u) == members - 1) {
       *grp = 0u;               // the group is complete: reset for the next launch
-      __threadfence_system();  // the group's stores before its count below
+      fence_acq_rel_gpu();  // the group's counts (this GPU) before the count below
       if (atomicAdd(done_ctr, 1u) == groups - 1) {
-        __threadfence_system();
+        fence_acq_rel_sys();
         const uint32_t step = *seq;
-        for (int d = 0; d < world; ++d) st_release_sys(peers.flags[d] + flag_base + rank, step);
+        for (int d = 0; d < world; ++d) st_relaxed_sys(peers.flags[d] + flag_base + rank, step);
         *done_ctr = 0u;
       }
     }

@@ -470,7 +470,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
       for (int i = threadIdx.x; i < world * E; i += blockDim.x) dst[i] = cnt[i];
     }
     __syncthreads();
-    if (threadIdx.x == 0) __threadfence_system();
+    if (threadIdx.x == 0) fence_acq_rel_sys();
     __syncthreads();
     if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, step);
     __syncthreads();
