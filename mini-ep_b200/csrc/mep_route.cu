@@ -460,23 +460,24 @@ __global__ void __launch_bounds__(kRouteThreads) k_route_fused(
         const int w0 = ((j - rr0) % nr + nr) % nr;
         cnt[d * E + e] = c > w0 ? (c - w0 - 1) / nr + 1 : 0;
       }
-      if (any_rep) rr[e] += c;
-      if (route_counts) route_counts[e] += c;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < world * E; i += blockDim.x) my_counts[i] = cnt[i];
+    // publish first (the peers wait for it), then the local bookkeeping
     for (int d = 0; d < world; ++d) {
       int32_t* dst = peers.cnt_in[d] + (int64_t)rank * world * E;
       for (int i = threadIdx.x; i < world * E; i += blockDim.x) dst[i] = cnt[i];
     }
     __syncthreads();
-    if (threadIdx.x == 0) fence_acq_rel_sys();
-    __syncthreads();
-    if (threadIdx.x < world) st_release_sys(peers.flags[threadIdx.x] + rank, step);
-    __syncthreads();
     if (threadIdx.x == 0) {
+      fence_acq_rel_sys();  // every thread's count stores (ordered by the barrier) before the flags
+      for (int d = 0; d < world; ++d) st_relaxed_sys(peers.flags[d] + rank, step);
       *seq = step;
       tl_mark(tl, kTlCountsSent);
+    }
+    for (int i = threadIdx.x; i < world * E; i += blockDim.x) my_counts[i] = cnt[i];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      if (any_rep) rr[e] += tot[e];
+      if (route_counts) route_counts[e] += tot[e];
     }
     // the receive layout, once every rank's counts are in
     extern __shared__ int route_dyn[];  // world * world * E counts for the layout pass
