@@ -441,7 +441,7 @@ class GraphedMoEBlock:
     """The MoE half of ``Block.forward`` (router + expert-parallel layer +
     residual, miniep/modeling.py:192-197) for a fixed token count, captured once
     into a CUDA graph over static device buffers and replayed per step: one
-    launch per layer step instead of ten, no host work in between.
+    launch per layer step instead of seven to nine, no host work in between.
 
     The step's sequence number lives on the device, so replays stay in lockstep
     with the other ranks exactly like eager calls. Every rank must construct
