@@ -215,29 +215,41 @@ __global__ void __launch_bounds__(THREADS, 1) k_router_tc(const __grid_constant_
         for (int e = 0; e < E; e += 4) lo[e / 4] = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
       }
       // top-k: larger value first, the lower expert index on ties. The
-      // rounds stay rolled (each CTA runs this code for a tile or two, so
-      // its instruction fetch, not its issue, is what costs); the scan over
-      // the E logits is unrolled to keep them in registers.
-      unsigned long long used = 0ull;
+      // logits are bf16 values, so each becomes one 32-bit key: its bf16
+      // bits mapped to an unsigned order (-0 taken as +0) above 0xFFFF - e.
+      // Keys are distinct and compare exactly as (value, then lower index),
+      // so each round is a max-tree over E keys (short dependency chains)
+      // instead of a serial scan. The rounds stay rolled: each CTA runs this
+      // code for a tile or two, so its instruction fetch is what costs.
+      uint32_t key[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        uint32_t b = __float_as_uint(v[e]) >> 16;
+        if ((b & 0x7FFFu) == 0u) b = 0u;
+        const uint32_t ord = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+        key[e] = (ord << 16) | (0xFFFFu - (uint32_t)e);
+      }
       float top0 = 0.f, ex_sum = 0.f;
       float ex[kMaxTopk];
 #pragma unroll 1
       for (int i = 0; i < a.k; ++i) {
-        float best = 0.f;
-        int bi = -1;
+        uint32_t t[E];
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const bool avail = ((used >> e) & 1ull) == 0ull;
-          if (avail && (bi < 0 || v[e] > best)) {
-            best = v[e];
-            bi = e;
-          }
-        }
-        used |= 1ull << bi;
+        for (int e = 0; e < E; ++e) t[e] = key[e];
+#pragma unroll
+        for (int w = E / 2; w > 0; w >>= 1)
+#pragma unroll
+          for (int e = 0; e < w; ++e) t[e] = max(t[e], t[e + w]);
+        const uint32_t top = t[0];
+#pragma unroll
+        for (int e = 0; e < E; ++e) key[e] = key[e] == top ? 0u : key[e];  // taken
+        const uint32_t ord = top >> 16;
+        const uint32_t b = (ord & 0x8000u) ? (ord & 0x7FFFu) : (~ord & 0xFFFFu);
+        const float best = __uint_as_float(b << 16);
         if (i == 0) top0 = best;
         ex[i] = expf(best - top0);
         ex_sum += ex[i];
-        a.idx_out[tok * a.k + i] = bi;
+        a.idx_out[tok * a.k + i] = (int64_t)(0xFFFFu - (top & 0xFFFFu));
       }
       const float rs = 1.f / ex_sum;
 #pragma unroll 1
