@@ -99,6 +99,8 @@ def parse():
                     help="steps of the per-stage timeline pass (0: skip)")
     ap.add_argument("--parity-rows", type=int, default=256, help="output rows checked per rank")
     ap.add_argument("--e2e-chunks", type=int, default=1, help="pieces per host batch in the e2e leg")
+    ap.add_argument("--e2e-warmup", type=int, default=20,
+                    help="untimed e2e steps before the timed ones (host copies, pipeline fill)")
     ap.add_argument("--e2e-depth", type=int, default=2,
                     help="device buffer sets the e2e leg's consecutive steps rotate through")
     ap.add_argument("--force-simt", action="store_true")
@@ -533,7 +535,7 @@ def main_b200(a):
             # around them; the timed region ends once the last copy out is done
             sblk(None, h_host, out_host, wait_output=False)
 
-        for _ in range(max(1, a.warmup)):
+        for _ in range(max(1, a.e2e_warmup)):
             e2e_step()
         torch.cuda.current_stream().wait_event(sblk.done)
         torch.cuda.synchronize()
@@ -541,8 +543,10 @@ def main_b200(a):
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
+        h0 = time.perf_counter()
         for _ in range(a.steps):
             e2e_step()
+        host_ms = (time.perf_counter() - h0) * 1e3 / a.steps  # enqueue time per step on the host
         torch.cuda.current_stream().wait_event(sblk.done)
         e1.record()
         torch.cuda.synchronize()
@@ -580,6 +584,10 @@ def main_b200(a):
         if world > 1:
             dist.all_reduce(tc, op=dist.ReduceOp.MAX)
         e2e["copies_only_ms_per_step"] = tc.item()
+        th = torch.tensor([host_ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(th, op=dist.ReduceOp.MAX)
+        e2e["host_enqueue_ms_per_step"] = th.item()
         del dbuf
         comm.check()
         del sblk
