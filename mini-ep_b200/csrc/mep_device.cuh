@@ -78,18 +78,27 @@ __device__ __forceinline__ void tl_end(uint64_t* tl, int slot) {
 
 // Spin until *flag has reached `target` (wrap-safe compare), for at most
 // wc.timeout_ns. Gives up early when another wait already failed, so one
-// missing peer costs one timeout rather than one per kernel. Returns true
-// when the flag arrived.
+// missing peer costs one timeout rather than one per kernel. The error word
+// lives in host memory: each read crosses PCIe, and thousands of waiting
+// threads reading it often would compete with the step's host copies, so a
+// thread reads it at most once per kErrPollNs. Returns true when the flag
+// arrived.
+constexpr unsigned long long kErrPollNs = 1000000ull;
 __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t target, int errcode,
                                           const WaitCfg& wc) {
   if ((int32_t)(ld_acquire_sys(flag) - target) >= 0) return true;
   const unsigned long long t0 = globaltimer_ns();
+  unsigned long long next_err = t0 + kErrPollNs;
   for (uint32_t it = 0;; ++it) {
     if ((int32_t)(ld_acquire_sys(flag) - target) >= 0) return true;
     __nanosleep(64);
     if ((it & 255u) == 255u) {
-      if (wc.err && *(volatile int*)wc.err != 0) return false;
-      if (globaltimer_ns() - t0 > wc.timeout_ns) {
+      const unsigned long long now = globaltimer_ns();
+      if (now >= next_err) {
+        if (wc.err && *(volatile int*)wc.err != 0) return false;
+        next_err = now + kErrPollNs;
+      }
+      if (now - t0 > wc.timeout_ns) {
         set_err(wc.err, errcode);
         return false;
       }
