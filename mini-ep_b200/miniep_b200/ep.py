@@ -356,17 +356,26 @@ class EPMoEBackend:
                                     ptr(w_in), ptr(w_out), n_local, ptr(out), st), ctx,
                   "mep_moe_forward")
         else:
+            # the reference's three timed phases (ep.py:223-235), as CUDA events
+            # for EPStats and as NVTX ranges for a profiler's timeline
+            nvtx = torch.cuda.nvtx
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
             ev[0].record()
+            nvtx.range_push(f"moe L{self.layer}: counts + dispatch")
             check(L.mep_route(ctx, self.layer, ptr(idx), ptr(valid), n, n_local, st), ctx,
                   "mep_route")
             check(L.mep_dispatch(ctx, ptr(x), ptr(idx), n, st), ctx, "mep_dispatch")
+            nvtx.range_pop()
             ev[1].record()
+            nvtx.range_push(f"moe L{self.layer}: experts")
             check(L.mep_expert_ffn(ctx, ptr(w_in), ptr(w_out), n_local, st), ctx,
                   "mep_expert_ffn")
+            nvtx.range_pop()
             ev[2].record()
+            nvtx.range_push(f"moe L{self.layer}: combine")
             check(L.mep_combine(ctx, ptr(gate), ptr(valid), n, None, 0.0, ptr(out), None, st),
                   ctx, "mep_combine")
+            nvtx.range_pop()
             ev[3].record()
             self.stats._pending.append(tuple(ev))
         return out
