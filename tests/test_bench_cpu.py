@@ -41,3 +41,18 @@ def test_reference_arm_other_ranks_print_nothing():
                          capture_output=True, text=True, timeout=300, env=env, cwd=REPO)
     assert out.returncode == 0, out.stderr[-2000:]
     assert not [l for l in out.stdout.splitlines() if l.startswith("{")]
+
+
+def test_ffn_traffic_is_the_capture_or_scaled_from_it():
+    """roofline.traffic: the ncu capture for the captured workload, else the
+    capture scaled by the algorithmic bytes, with the source stated."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", REPO / "bench.py")
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    base = b.FFN_ALG_BYTES[("a", 16384)]
+    t, src = b.ffn_traffic("a", 16384, 1, base)
+    assert t == b.FFN_DRAM_BYTES[("a", 16384)] and "capture of this workload" in src
+    t8, src8 = b.ffn_traffic("a", 16384, 8, base / 8)
+    assert abs(t8 - t / 8) < 1e-3 * t and "scaled" in src8
+    assert b.ffn_traffic("b", 16384, 1, 1e9)[0] is None
